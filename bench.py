@@ -1,0 +1,365 @@
+"""Benchmark: Mamba2 SSD layer forward tokens/s on B200 (one process per GPU).
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+A "step" is one SSD layer forward over one synthetic batch of the config (default c2,
+the nemotron-h-8b shape the north star targets: b=1, L=4096, H=128, P=64, G=8, N=128,
+Q=128, bf16 inputs, initial states in, final states out).  At N GPUs every rank runs its
+own batch (weak scaling, no data-path collective).  `value` is measured with inputs
+resident in HBM (one CUDA graph per step, input sets rotated so consecutive steps share
+no L2 lines); `e2e` goes through the public Python API with pinned host buffers and
+host<->device copies inside the timed region.  `--impl reference` times the CPU
+restatement of the reference algorithm (the reference itself needs JAX, absent here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+_REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(_REPO, "mamba2-jax-pallas_b200"))
+sys.path.insert(0, _REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from mamba2_b200 import synthetic as S  # noqa: E402
+
+N_SETS = 4   # rotated input sets (each > L2 when combined with its output)
+
+
+def _peaks():
+    try:
+        with open(os.path.join(_REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def layer_work(cfg):
+    """Algorithmic FLOPs and HBM bytes of one SSD layer forward (causal FLOPs; fp32 out)."""
+    b, L, H, P, G, N, Q = (cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.ngroups,
+                           cfg.dstate, cfg.chunk_size)
+    nc = cfg.nchunks
+    tri = Q * (Q + 1) / 2
+    flops = 2 * b * (nc * G * tri * N + L * H * P * N + nc * H * tri * P + L * H * N * P
+                     + nc * H * P * N)
+    isz = 2 if cfg.dtype == "bf16" else 4
+    byts = b * L * (H * P + H + 2 * G * N) * isz + b * L * H * P * 4
+    if cfg.has_z:
+        byts += b * L * H * P * isz
+    if cfg.has_init:
+        byts += b * H * P * N * 4
+    if cfg.return_final:
+        byts += b * H * P * N * 4
+    return flops, byts
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-i", str(index), "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) >= 9:
+                    rows.append(c)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dev_inputs(inp, cfg, device):
+    tdt = torch.bfloat16 if cfg.dtype == "bf16" else torch.float32
+    d = {}
+    for k in ("x", "dt", "B", "C", "z"):
+        d[k] = None if inp[k] is None else torch.from_numpy(inp[k]).to(device=device, dtype=tdt)
+    for k in ("A", "D", "dt_bias", "initial_states"):
+        d[k] = None if inp[k] is None else torch.from_numpy(inp[k]).to(device)
+    for k in ("seq_idx", "cu_seqlens"):
+        d[k] = None if inp[k] is None else torch.from_numpy(inp[k]).to(device=device, dtype=torch.int32)
+    return d
+
+
+def fwd_kwargs(cfg, d):
+    return dict(D=d["D"], z=d["z"], dt_bias=d["dt_bias"], initial_states=d["initial_states"],
+                seq_idx=d["seq_idx"], cu_seqlens=d["cu_seqlens"], dt_softplus=True,
+                return_final_states=cfg.return_final)
+
+
+def time_region(fn, steps, stream):
+    """Device time of `steps` calls of fn() between two events on `stream`."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def time_kernel(fn, reps=20):
+    """Average device time of one launch: a sleep kernel ahead of each start event keeps
+    host launch overhead out of the event window."""
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    tot = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2_000_000)
+        e0.record(s)
+        fn()
+        e1.record(s)
+        e1.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / reps
+
+
+def kernel_breakdown(cfg, d, runner):
+    """Per-kernel device times (ms), algorithmic bytes and FLOPs of one forward."""
+    from mamba2_b200 import kernels as K
+    b, L, H, P, G, N, Q = (cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.ngroups,
+                           cfg.dstate, cfg.chunk_size)
+    nc = cfg.nchunks
+    isz = 2 if cfg.dtype == "bf16" else 4
+    res = []
+    if runner.uses_tc:
+        flops, byts = layer_work(cfg)
+        ms = time_kernel(lambda: runner())
+        res.append(("ssd_fused_tc", ms, byts, flops, "tensor" if flops / 1.6e15 > byts / 6.5e12 else "hbm"))
+        return res
+    dA, dto = K.chunk_cumsum_fwd(d["dt"], d["A"], Q, dt_bias=d["dt_bias"], dt_softplus=True)
+    st = K.chunk_state_fwd(d["x"], d["B"], dto, dA, seq_idx=d["seq_idx"])
+    cb = K.bmm_chunk_fwd(d["C"], d["B"], Q, seq_idx=d["seq_idx"])
+    dAc = dA[..., -1].contiguous()
+    csz = b * H * nc * Q * 4
+    ssz = b * nc * H * P * N * 4
+    res.append(("chunk_cumsum", time_kernel(lambda: K.chunk_cumsum_fwd(d["dt"], d["A"], Q, dt_bias=d["dt_bias"], dt_softplus=True)),
+                b * L * H * isz + 2 * csz, 0, "hbm"))
+    res.append(("chunk_state", time_kernel(lambda: K.chunk_state_fwd(d["x"], d["B"], dto, dA, seq_idx=d["seq_idx"])),
+                b * L * (H * P + G * N) * isz + 2 * csz + ssz, 2 * b * L * H * P * N, "hbm"))
+    res.append(("state_passing", time_kernel(lambda: K.state_passing_fwd(st.view(b, nc, H, P * N), dAc,
+                                                                          seq_idx=d["seq_idx"], chunk_size=Q)),
+                2 * ssz, 0, "hbm"))
+    res.append(("bmm_chunk", time_kernel(lambda: K.bmm_chunk_fwd(d["C"], d["B"], Q, seq_idx=d["seq_idx"])),
+                2 * b * L * G * N * isz + b * nc * G * Q * Q * 4, 2 * b * nc * G * Q * Q * N, "hbm"))
+    res.append(("chunk_scan", time_kernel(lambda: K.chunk_scan_fwd(cb, d["x"], dto, dA, d["C"], st, D=d["D"], z=d["z"],
+                                                                  seq_idx=d["seq_idx"])),
+                b * nc * G * Q * Q * 4 + b * L * (H * P + G * N) * isz + 2 * csz + ssz + b * L * H * P * 4,
+                2 * b * nc * H * (Q * (Q + 1) / 2 * P + Q * N * P), "hbm"))
+    return res
+
+
+def cpu_oracle_sample(cfg, budget_s=12.0, heads=None):
+    """Time the CPU restatement (numpy float64, BLAS on all host threads) on a head slice of
+    the workload; returns (tokens/s scaled to the full head count, description, threads)."""
+    from oracle import ssd_ref as R
+    threads = len(os.sched_getaffinity(0))
+    hs = heads or max(cfg.ngroups, min(cfg.nheads, 16))
+    hs -= hs % cfg.ngroups
+    small = S.scaled(cfg, nheads=hs)
+    inp = S.make_ssd_inputs(small, 99)
+    reps, t_tot = 0, 0.0
+    while t_tot < budget_s and reps < 50:
+        t0 = time.perf_counter()
+        R.ssd_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], cfg.chunk_size,
+                       D=inp["D"], z=inp["z"], dt_bias=inp["dt_bias"],
+                       initial_states=inp["initial_states"], seq_idx=inp["seq_idx"],
+                       dt_softplus=True, return_final_states=cfg.return_final)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    t = t_tot / reps
+    tok_s = cfg.tokens / (t * cfg.nheads / hs)
+    desc = (f"oracle/ssd_ref.py (numpy float64 restatement of ops/ssd_naive.py) on {hs} of "
+            f"{cfg.nheads} heads, {reps} reps x {t:.2f}s, scaled by heads")
+    return tok_s, desc, threads
+
+
+def run_reference(args, cfg, rank):
+    if rank != 0:
+        return
+    flops, byts = layer_work(cfg)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_oracle_sample(cfg, budget_s=0.0)
+    t_all = 0.0
+    for _ in range(args.steps):
+        v, desc, thr = cpu_oracle_sample(cfg, budget_s=0.0)
+        vals.append(v)
+        t_all += cfg.tokens / v
+    value = args.steps * cfg.tokens / t_all
+    line = {"impl": "reference", "metric": "SSD layer fwd tokens/s", "value": value,
+            "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t_all / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch,
+                       "seqlen": cfg.seqlen, "nheads": cfg.nheads, "headdim": cfg.headdim,
+                       "ngroups": cfg.ngroups, "dstate": cfg.dstate, "chunk_size": cfg.chunk_size,
+                       "input_dtype": cfg.dtype},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": thr, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "the reference (JAX/Pallas) is not installable here; its algorithm is timed "
+                    "through the CPU restatement"}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, cfg, rank, world, device):
+    from mamba2_b200 import mamba_chunk_scan_combined_fwd
+    from mamba2_b200.runner import SsdForward
+    hbm, tfl, peak_kind = _peaks()
+    inp = S.make_ssd_inputs(cfg, 1000 + 2 + rank)
+    sets = [dev_inputs(inp, cfg, device) for _ in range(N_SETS)]
+    runners = [SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], cfg.chunk_size, **fwd_kwargs(cfg, d))
+               for d in sets]
+    graphs = [r.graph() for r in runners]
+    stream = torch.cuda.current_stream()
+    for i in range(max(args.warmup, 3)):
+        graphs[i % N_SETS].replay()
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(lambda i: graphs[i % N_SETS].replay(), args.steps, stream)
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = clk.stop() if clk else None
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    value = args.steps * cfg.tokens * world / (ms / 1e3)
+    launches_per_step = runners[0].launches_per_step
+
+    # end to end through the public API: pinned host inputs -> device -> forward -> host
+    host = {k: (None if v is None else v.cpu().pin_memory()) for k, v in sets[0].items()}
+    h2d = sum(v.numel() * v.element_size() for k, v in host.items() if v is not None)
+    b, L, H, P, N = cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.dstate
+    out_h = torch.empty((b, L, H, P), dtype=torch.float32).pin_memory()
+    fin_h = torch.empty((b, H, P, N), dtype=torch.float32).pin_memory() if cfg.return_final else None
+    d2h = out_h.numel() * 4 + (fin_h.numel() * 4 if fin_h is not None else 0)
+    ws = torch.empty(runners[0].workspace.numel(), device=device, dtype=torch.uint8)
+
+    def e2e_step(_i):
+        dd = {k: (None if v is None else v.to(device, non_blocking=True)) for k, v in host.items()}
+        r = mamba_chunk_scan_combined_fwd(dd["x"], dd["dt"], dd["A"], dd["B"], dd["C"], cfg.chunk_size,
+                                          workspace=ws, **fwd_kwargs(cfg, dd))
+        if cfg.return_final:
+            out_h.copy_(r[0], non_blocking=True)
+            fin_h.copy_(r[1], non_blocking=True)
+        else:
+            out_h.copy_(r, non_blocking=True)
+    for i in range(2):
+        e2e_step(i)
+    if world > 1:
+        torch.distributed.barrier()
+    ms_e2e = time_region(e2e_step, args.steps, stream)
+    t = torch.tensor([ms_e2e], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_val = args.steps * cfg.tokens * world / (float(t.item()) / 1e3)
+
+    if rank != 0:
+        return
+    brk = kernel_breakdown(cfg, sets[0], runners[0])
+    top = max(brk, key=lambda r: r[1])
+    name, kms, kbytes, kflops, bound = top
+    if bound == "tensor":
+        ach, peak, unit = kflops / (kms / 1e3) / 1e12, tfl, "TFLOP/s"
+    else:
+        ach, peak, unit = kbytes / (kms / 1e3) / 1e9, hbm, "GB/s"
+    flops, byts = layer_work(cfg)
+    t_roof = max(flops / (tfl * 1e12), byts / (hbm * 1e9))
+    line = {"metric": "SSD layer fwd tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "bf16" else "f32",
+            "data": "synthetic",
+            "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch, "seqlen": cfg.seqlen,
+                       "nheads": cfg.nheads, "headdim": cfg.headdim, "ngroups": cfg.ngroups,
+                       "dstate": cfg.dstate, "chunk_size": cfg.chunk_size, "input_dtype": cfg.dtype,
+                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "l2": f"{N_SETS} rotated input sets, each step's inputs+outputs > L2"},
+            "roofline": {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+                         "frac": ach / peak, "peak_kind": peak_kind, "traffic": None,
+                         "kernel_ms": kms},
+            "layer_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": 1e3 * ms / args.steps,
+                               "frac": t_roof / (ms / args.steps / 1e3), "flops": flops, "bytes": byts},
+            "kernels": {r[0]: round(r[1] * 1e3, 2) for r in brk},
+            "e2e": {"value": e2e_val, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks}
+    if world == 1 and not args.no_cpu_baseline:
+        v, desc, thr = cpu_oracle_sample(cfg)
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port",
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = S.CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank)
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=device)
+    try:
+        run_ours(args, cfg, rank, world, device)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+/*
+ * ssd_b200.h — C ABI of the B200 (sm_100a) Mamba2 SSD forward and decode-step kernels.
+ *
+ * This is the drop-in boundary.  Each entry point replaces one function of the
+ * reference's hot path (AlexG1105/mamba2-jax-pallas, cited as path:line below) and is
+ * what a jax.ffi handler, a ctypes binding or a C++ caller binds.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers; every tensor is dense row-major ("contiguous") in the
+ *     documented layout.  Dims use the reference's names: b=batch, L=seqlen,
+ *     H=nheads, P=headdim, G=ngroups, N=dstate, Q=chunk_size, nc=ceil(L/Q).
+ *     Head h reads group h / (H/G).
+ *   - Input tensors x, B, C, z (and dt, separately) are SSD_DTYPE_F32 or
+ *     SSD_DTYPE_BF16; A, D, dt_bias, initial_states and every output are float32.
+ *   - Work is enqueued on `stream`; nothing blocks the host and nothing allocates
+ *     device memory.  Scratch memory, where needed, is caller-provided
+ *     (`workspace`, size from the matching *_workspace_bytes()).
+ *   - The return value is an ssd_status_t; on failure ssd_last_error() returns a
+ *     thread-local message.  Shape/pointer errors are reported before any launch.
+ *   - Calls on one stream are ordered; concurrent calls on different streams must
+ *     not share output or workspace buffers.
+ */
+#ifndef SSD_B200_H_
+#define SSD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SSD_B200_ABI_VERSION 1
+
+typedef enum ssd_status {
+  SSD_OK = 0,
+  SSD_ERR_INVALID_ARG = 1,   /* bad shape, null pointer, inconsistent dims */
+  SSD_ERR_UNSUPPORTED = 2,   /* valid but not implemented (e.g. dtype combination) */
+  SSD_ERR_ALIGNMENT = 3,     /* pointer not aligned as the kernel requires */
+  SSD_ERR_WORKSPACE = 4,     /* workspace null or too small */
+  SSD_ERR_CUDA = 5,          /* a CUDA launch or runtime call failed */
+  SSD_ERR_TIMEOUT = 6        /* a bounded inter-CTA wait gave up (device status word) */
+} ssd_status_t;
+
+typedef enum ssd_dtype {
+  SSD_DTYPE_F32 = 0,
+  SSD_DTYPE_BF16 = 1
+} ssd_dtype_t;
+
+/* Opaque CUDA stream (cudaStream_t); 0 = legacy default stream. */
+typedef void* ssd_stream_t;
+
+/* Parameters of the combined forward.  Optional pointers may be NULL. */
+typedef struct ssd_fwd_params {
+  int64_t batch, seqlen, nheads, headdim, ngroups, dstate, chunk_size;
+  int32_t dtype;          /* ssd_dtype_t of x, B, C, z */
+  int32_t dt_dtype;       /* ssd_dtype_t of dt */
+  int32_t dt_softplus;    /* nonzero: dt <- (dt <= 20 ? log1p(exp(dt)) : dt) after bias */
+  int32_t D_ndim;         /* 0: no D, 1: D is (H,), 2: D is (H,P) */
+  float dt_min, dt_max;   /* clamp applied after softplus (use +INFINITY for no max) */
+  int32_t num_seqs;       /* entries of cu_seqlens minus one (varlen states only) */
+  int32_t flags;          /* SSD_FLAG_* */
+  /* inputs */
+  const void* x;          /* (b,L,H,P) */
+  const void* dt;         /* (b,L,H) */
+  const float* A;         /* (H,) */
+  const void* B;          /* (b,L,G,N) */
+  const void* C;          /* (b,L,G,N) */
+  const float* D;         /* (H,) or (H,P) */
+  const void* z;          /* (b,L,H,P) gate: out *= z*sigmoid(z) */
+  const float* dt_bias;   /* (H,) */
+  const float* initial_states; /* (b,H,P,N) */
+  const int32_t* seq_idx;      /* (b,L) packed-sequence ids */
+  const int32_t* cu_seqlens;   /* (num_seqs+1,), requires batch == 1 */
+  /* outputs */
+  float* out;             /* (b,L,H,P), required */
+  float* out_x;           /* (b,L,H,P) pre-gate output (only with z) */
+  float* final_states;    /* (b,H,P,N) */
+  float* varlen_states;   /* (num_seqs,H,P,N), requires cu_seqlens */
+  float* dA_cumsum;       /* optional copy-out of stage-1 results, (b,H,nc,Q) */
+  float* dt_out;          /* (b,H,nc,Q) */
+} ssd_fwd_params_t;
+
+/* flags */
+#define SSD_FLAG_FORCE_SIMT   1  /* use the fp32 CUDA-core pipeline even for bf16 inputs */
+#define SSD_FLAG_ROUND_STATES 2  /* round passed chunk states to the input dtype before
+                                    chunk_scan, as ssd_combined.py:140 does */
+
+/* Bytes of device workspace ssd_combined_fwd needs for these params. */
+size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p);
+
+/* 1 if ssd_combined_fwd runs the tcgen05 tensor-core pipeline for these params, else 0
+ * (fp32 CUDA-core pipeline).  No reference counterpart: introspection for callers that
+ * size graphs or report which path ran. */
+int ssd_combined_uses_tensor_cores(const ssd_fwd_params_t* p);
+
+/* Number of kernel launches one ssd_combined_fwd call enqueues for these params.
+ * No reference counterpart (introspection). */
+int ssd_combined_num_launches(const ssd_fwd_params_t* p);
+
+/* Combined SSD forward.
+ * Replaces mamba_chunk_scan_combined_fwd (src/mamba2_jax/kernels/ssd_combined.py:46-203)
+ * and, as its fallback target, mamba_chunk_scan_combined_naive
+ * (src/mamba2_jax/ops/ssd_naive.py:325-397). */
+int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspace_bytes,
+                     ssd_stream_t stream);
+
+/* Stage 1.  Replaces chunk_cumsum_fwd (src/mamba2_jax/kernels/chunk_cumsum_fwd.py:288-302,
+ * :194-235).  dt (b,L,H) -> dA_cumsum, dt_out (b,H,nc,Q) float32.  Padded tail
+ * positions (>= L) get dt_out = 0, as the kernel path does (:228-231). */
+int ssd_chunk_cumsum_fwd(const void* dt, int32_t dt_dtype, const float* A, const float* dt_bias,
+                         int32_t dt_softplus, float dt_min, float dt_max,
+                         int64_t batch, int64_t seqlen, int64_t nheads, int64_t chunk_size,
+                         float* dA_cumsum, float* dt_out, ssd_stream_t stream);
+
+/* Stage 2.  Replaces chunk_state_fwd (src/mamba2_jax/kernels/chunk_state_fwd.py:424-441,
+ * preprocess :194-304).  states (b,nc,H,P,N) float32. */
+int ssd_chunk_state_fwd(const void* x, const void* B, int32_t dtype,
+                        const float* dt_out, const float* dA_cumsum, const int32_t* seq_idx,
+                        int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                        int64_t ngroups, int64_t dstate, int64_t chunk_size,
+                        float* states, ssd_stream_t stream);
+
+/* Stage 3.  Replaces state_passing_fwd (src/mamba2_jax/kernels/state_passing_fwd.py:348-363,
+ * :158-341).  states (b,nc,H,dim) float32; dA_chunk_cumsum is read at
+ * dA_chunk[(bi*H + h)*stride_bh + c*stride_c] (for a (b,H,nc) array: stride_bh = nc,
+ * stride_c = 1).  out (b,nc,H,dim) in out_dtype (may alias states), final (b,H,dim) f32.
+ * seq_idx (b,seqlen) needs chunk_size. */
+int ssd_state_passing_fwd(const float* states, const float* dA_chunk, int64_t stride_bh,
+                          int64_t stride_c, const float* initial_states, const int32_t* seq_idx,
+                          int64_t batch, int64_t nchunks, int64_t nheads, int64_t dim,
+                          int64_t seqlen, int64_t chunk_size,
+                          void* out, int32_t out_dtype, float* final_states,
+                          ssd_stream_t stream);
+
+/* Stage 4.  Replaces bmm_chunk_fwd (src/mamba2_jax/kernels/bmm_chunk_fwd.py:381-400,
+ * :293-374).  out[b,c,g,m,n] = sum_k a[b,cQ+m,g,k] * b[b,cQ+n,g,k], (b,nc,G,Q,Q) f32;
+ * seq_idx mask and optional causal (lower-triangular) mask. */
+int ssd_bmm_chunk_fwd(const void* a, const void* b, int32_t dtype, const int32_t* seq_idx,
+                      int32_t causal, int64_t batch, int64_t seqlen, int64_t ngroups,
+                      int64_t k, int64_t chunk_size, float* out, ssd_stream_t stream);
+
+/* Stage 5.  Replaces chunk_scan_fwd (src/mamba2_jax/kernels/chunk_scan_fwd.py:579-600,
+ * :482-572).  cb (b,nc,G,Q,Q) f32; states = passed states (b,nc,H,P,N) in states_dtype.
+ * out / out_x (b,L,H,P) f32. */
+int ssd_chunk_scan_fwd(const float* cb, const void* x, int32_t dtype, const float* dt_out,
+                       const float* dA_cumsum, const void* C, const void* states,
+                       int32_t states_dtype, const float* D, int32_t D_ndim, const void* z,
+                       const int32_t* seq_idx,
+                       int64_t batch, int64_t seqlen, int64_t nheads, int64_t headdim,
+                       int64_t ngroups, int64_t dstate, int64_t chunk_size,
+                       float* out, float* out_x, ssd_stream_t stream);
+
+/* Varlen final states.  Replaces chunk_state_varlen_mosaic
+ * (src/mamba2_jax/kernels/chunk_state_fwd.py:448-597).  B (T,G,N), x (T,H,P) in dtype;
+ * dt_out, dA_cumsum (H,nc,Q); chunk_states = passed states (nc,H,P,N) in states_dtype;
+ * out (num_seqs,H,P,N) f32. */
+int ssd_chunk_state_varlen_fwd(const void* B, const void* x, int32_t dtype,
+                               const float* dt_out, const float* dA_cumsum,
+                               const int32_t* cu_seqlens, int32_t num_seqs,
+                               const void* chunk_states, int32_t states_dtype,
+                               int64_t total_seqlen, int64_t nheads, int64_t headdim,
+                               int64_t ngroups, int64_t dstate, int64_t chunk_size,
+                               float* out, ssd_stream_t stream);
+
+/* Parameters of the single-token decode step. */
+typedef struct ssu_params {
+  int64_t batch, nheads, headdim, ngroups, dstate;
+  int32_t dtype;          /* ssd_dtype_t of x, z, B, C */
+  int32_t dt_dtype;       /* ssd_dtype_t of dt */
+  int32_t dt_ndim;        /* 2: dt (b,H); 3: dt (b,H,P) */
+  int32_t A_ndim;         /* 1: A (H,); 3: A (H,P,N) */
+  int32_t D_ndim;         /* 0, 1 (H,) or 2 (H,P) */
+  int32_t dt_bias_ndim;   /* 0, 1 (H,) or 2 (H,P) */
+  int32_t dt_softplus;    /* nonzero: dt <- log(1 + exp(dt)) after bias */
+  int32_t reserved;
+  float* state;           /* (b,H,P,N) f32, updated IN PLACE */
+  const void* x;          /* (b,H,P) */
+  const void* dt;
+  const float* A;
+  const void* B;          /* (b,G,N) */
+  const void* C;          /* (b,G,N) */
+  const float* D;
+  const void* z;          /* (b,H,P) or NULL */
+  const float* dt_bias;
+  float* out;             /* (b,H,P) f32 */
+} ssu_params_t;
+
+/* Decode step.  Replaces selective_state_update
+ * (src/mamba2_jax/ops/selective_state_update.py:22-123); the state is updated in place
+ * instead of returned as a new array. */
+int ssd_selective_state_update(const ssu_params_t* p, ssd_stream_t stream);
+
+/* Thread-local description of the last failure on this host thread ("" if none). */
+const char* ssd_last_error(void);
+
+/* SSD_B200_ABI_VERSION of the loaded library. */
+int ssd_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSD_B200_H_ */

@@ -1,0 +1,274 @@
+// C ABI entry points (include/ssd_b200.h): argument validation, workspace carving and
+// stage orchestration.  No entry point allocates device memory or blocks the host.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "ssd_kernels.h"
+#include "ssd_tc.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return SSD_OK;
+  return fail(SSD_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+bool dtype_ok(int d) { return d == SSD_DTYPE_F32 || d == SSD_DTYPE_BF16; }
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int check_dims(int64_t b, int64_t L, int64_t H, int64_t P, int64_t G, int64_t N, int64_t Q) {
+  if (b <= 0 || L <= 0 || H <= 0 || P <= 0 || G <= 0 || N <= 0 || Q <= 0)
+    return fail(SSD_ERR_INVALID_ARG, "dims must be positive (b=%lld L=%lld H=%lld P=%lld G=%lld N=%lld Q=%lld)",
+                (long long)b, (long long)L, (long long)H, (long long)P, (long long)G, (long long)N, (long long)Q);
+  if (H % G != 0) return fail(SSD_ERR_INVALID_ARG, "nheads (%lld) must be a multiple of ngroups (%lld)", (long long)H, (long long)G);
+  if (Q % 32 != 0 || Q > 256)
+    return fail(SSD_ERR_UNSUPPORTED, "chunk_size %lld unsupported (need a multiple of 32, <= 256)", (long long)Q);
+  return SSD_OK;
+}
+
+struct Workspace {
+  size_t dA, dt, states, passed_lp, cb, total;
+};
+
+Workspace plan_ws(const ssd_fwd_params_t* p) {
+  const int64_t nc = (p->seqlen + p->chunk_size - 1) / p->chunk_size;
+  const size_t cs = (size_t)p->batch * p->nheads * nc * p->chunk_size * sizeof(float);
+  const size_t st = (size_t)p->batch * nc * p->nheads * p->headdim * p->dstate * sizeof(float);
+  const size_t cb = (size_t)p->batch * nc * p->ngroups * p->chunk_size * p->chunk_size * sizeof(float);
+  Workspace w;
+  size_t off = 0;
+  w.dA = off; off += align256(cs);
+  w.dt = off; off += align256(cs);
+  w.states = off; off += align256(st);
+  w.passed_lp = off;
+  if ((p->flags & SSD_FLAG_ROUND_STATES) && p->dtype == SSD_DTYPE_BF16) off += align256(st / 2);
+  w.cb = off; off += align256(cb);
+  w.total = off;
+  return w;
+}
+
+int validate_fwd(const ssd_fwd_params_t* p) {
+  if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
+  int s = check_dims(p->batch, p->seqlen, p->nheads, p->headdim, p->ngroups, p->dstate, p->chunk_size);
+  if (s) return s;
+  if (!dtype_ok(p->dtype) || !dtype_ok(p->dt_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (!p->x || !p->dt || !p->A || !p->B || !p->C || !p->out)
+    return fail(SSD_ERR_INVALID_ARG, "x, dt, A, B, C and out are required");
+  if (p->D_ndim < 0 || p->D_ndim > 2 || (p->D_ndim && !p->D)) return fail(SSD_ERR_INVALID_ARG, "bad D_ndim / D");
+  if (p->out_x && !p->z) return fail(SSD_ERR_INVALID_ARG, "out_x requires z");
+  if (p->varlen_states) {
+    if (!p->cu_seqlens || p->num_seqs <= 0) return fail(SSD_ERR_INVALID_ARG, "varlen_states requires cu_seqlens and num_seqs > 0");
+    if (p->batch != 1) return fail(SSD_ERR_INVALID_ARG, "cu_seqlens for varlen states is only supported with batch=1");
+  }
+  if (std::isnan(p->dt_min) || std::isnan(p->dt_max) || p->dt_min > p->dt_max)
+    return fail(SSD_ERR_INVALID_ARG, "bad dt_limit");
+  return SSD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ssd_last_error(void) { return g_err; }
+
+int ssd_abi_version(void) { return SSD_B200_ABI_VERSION; }
+
+size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p) {
+  if (!p) return 0;
+  const size_t tc = ssd::tc_workspace_bytes(p);
+  const size_t simt = plan_ws(p).total;
+  return tc > simt ? tc : simt;
+}
+
+int ssd_combined_uses_tensor_cores(const ssd_fwd_params_t* p) {
+  return (p && validate_fwd(p) == SSD_OK && !(p->flags & SSD_FLAG_FORCE_SIMT) && ssd::tc_supported(p)) ? 1 : 0;
+}
+
+int ssd_combined_num_launches(const ssd_fwd_params_t* p) {
+  if (!p || validate_fwd(p) != SSD_OK) return 0;
+  if (ssd_combined_uses_tensor_cores(p)) return ssd::tc_num_launches(p);
+  return 5 + (p->varlen_states ? 1 : 0);
+}
+
+int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspace_bytes,
+                     ssd_stream_t stream_) {
+  g_err[0] = 0;
+  int s = validate_fwd(p);
+  if (s) return s;
+  cudaStream_t st = (cudaStream_t)stream_;
+  const size_t need = ssd_combined_workspace_bytes(p);
+  if (!workspace || workspace_bytes < need)
+    return fail(SSD_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", need, workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(SSD_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+
+  // Tensor-core pipeline for bf16 inputs when the shape is one it covers.
+  if (!(p->flags & SSD_FLAG_FORCE_SIMT) && ssd::tc_supported(p)) {
+    return ssd::tc_combined_fwd(p, workspace, st) ;
+  }
+
+  const Workspace w = plan_ws(p);
+  char* ws = (char*)workspace;
+  const int64_t b = p->batch, L = p->seqlen, H = p->nheads, P = p->headdim, G = p->ngroups,
+                N = p->dstate, Q = p->chunk_size, nc = (L + Q - 1) / Q;
+  float* dA = p->dA_cumsum ? p->dA_cumsum : (float*)(ws + w.dA);
+  float* dt = p->dt_out ? p->dt_out : (float*)(ws + w.dt);
+  float* states = (float*)(ws + w.states);
+  float* cb = (float*)(ws + w.cb);
+  const bool lp = (p->flags & SSD_FLAG_ROUND_STATES) && p->dtype == SSD_DTYPE_BF16;
+  void* passed = lp ? (void*)(ws + w.passed_lp) : (void*)states;
+  const int passed_dtype = lp ? SSD_DTYPE_BF16 : SSD_DTYPE_F32;
+
+  if ((s = cuda_status(ssd::launch_chunk_cumsum(p->dt, p->dt_dtype, p->A, p->dt_bias, p->dt_softplus,
+                                                p->dt_min, p->dt_max, b, L, H, Q, dA, dt, st), "chunk_cumsum")))
+    return s;
+  if ((s = cuda_status(ssd::launch_chunk_state(p->x, p->B, p->dtype, dt, dA, p->seq_idx, b, L, H, P, G, N, Q,
+                                               states, st), "chunk_state")))
+    return s;
+  if ((s = cuda_status(ssd::launch_state_passing(states, dA + (Q - 1), nc * Q, Q, p->initial_states, p->seq_idx,
+                                                 b, nc, H, P * N, L, Q, passed, passed_dtype,
+                                                 p->final_states, st), "state_passing")))
+    return s;
+  if ((s = cuda_status(ssd::launch_bmm_chunk(p->C, p->B, p->dtype, p->seq_idx, 0, b, L, G, N, Q, cb, st),
+                       "bmm_chunk")))
+    return s;
+  if ((s = cuda_status(ssd::launch_chunk_scan(cb, p->x, p->dtype, dt, dA, p->C, passed, passed_dtype, p->D,
+                                              p->D_ndim, p->z, p->seq_idx, b, L, H, P, G, N, Q, p->out,
+                                              p->out_x, st), "chunk_scan")))
+    return s;
+  if (p->varlen_states) {
+    if ((s = cuda_status(ssd::launch_chunk_state_varlen(p->B, p->x, p->dtype, dt, dA, p->cu_seqlens, p->num_seqs,
+                                                        passed, passed_dtype, L, H, P, G, N, Q,
+                                                        p->varlen_states, st), "chunk_state_varlen")))
+      return s;
+  }
+  return SSD_OK;
+}
+
+int ssd_chunk_cumsum_fwd(const void* dt, int32_t dt_dtype, const float* A, const float* dt_bias,
+                         int32_t dt_softplus, float dt_min, float dt_max, int64_t batch, int64_t seqlen,
+                         int64_t nheads, int64_t chunk_size, float* dA_cumsum, float* dt_out,
+                         ssd_stream_t stream) {
+  g_err[0] = 0;
+  int s = check_dims(batch, seqlen, nheads, 1, 1, 1, chunk_size);
+  if (s) return s;
+  if (!dt || !A || !dA_cumsum || !dt_out) return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(dt_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  return cuda_status(ssd::launch_chunk_cumsum(dt, dt_dtype, A, dt_bias, dt_softplus, dt_min, dt_max, batch,
+                                              seqlen, nheads, chunk_size, dA_cumsum, dt_out,
+                                              (cudaStream_t)stream), "chunk_cumsum");
+}
+
+int ssd_chunk_state_fwd(const void* x, const void* B, int32_t dtype, const float* dt_out,
+                        const float* dA_cumsum, const int32_t* seq_idx, int64_t batch, int64_t seqlen,
+                        int64_t nheads, int64_t headdim, int64_t ngroups, int64_t dstate,
+                        int64_t chunk_size, float* states, ssd_stream_t stream) {
+  g_err[0] = 0;
+  int s = check_dims(batch, seqlen, nheads, headdim, ngroups, dstate, chunk_size);
+  if (s) return s;
+  if (!x || !B || !dt_out || !dA_cumsum || !states) return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  return cuda_status(ssd::launch_chunk_state(x, B, dtype, dt_out, dA_cumsum, seq_idx, batch, seqlen, nheads,
+                                             headdim, ngroups, dstate, chunk_size, states,
+                                             (cudaStream_t)stream), "chunk_state");
+}
+
+int ssd_state_passing_fwd(const float* states, const float* dA_chunk, int64_t stride_bh, int64_t stride_c,
+                          const float* initial_states, const int32_t* seq_idx, int64_t batch,
+                          int64_t nchunks, int64_t nheads, int64_t dim, int64_t seqlen, int64_t chunk_size,
+                          void* out, int32_t out_dtype, float* final_states, ssd_stream_t stream) {
+  g_err[0] = 0;
+  if (batch <= 0 || nchunks <= 0 || nheads <= 0 || dim <= 0)
+    return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
+  if (!states || !dA_chunk || !out) return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(out_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (seq_idx) {
+    if (chunk_size <= 0 || seqlen <= 0) return fail(SSD_ERR_INVALID_ARG, "seq_idx requires chunk_size and seqlen");
+    if ((seqlen + chunk_size - 1) / chunk_size != nchunks)
+      return fail(SSD_ERR_INVALID_ARG, "ceil(seqlen/chunk_size) != nchunks");
+  }
+  if (out_dtype != SSD_DTYPE_F32 && (const void*)out == (const void*)states)
+    return fail(SSD_ERR_INVALID_ARG, "out may alias states only for float32 output");
+  return cuda_status(ssd::launch_state_passing(states, dA_chunk, stride_bh, stride_c, initial_states, seq_idx,
+                                               batch, nchunks, nheads, dim, seqlen, chunk_size, out, out_dtype,
+                                               final_states, (cudaStream_t)stream), "state_passing");
+}
+
+int ssd_bmm_chunk_fwd(const void* a, const void* b, int32_t dtype, const int32_t* seq_idx, int32_t causal,
+                      int64_t batch, int64_t seqlen, int64_t ngroups, int64_t k, int64_t chunk_size,
+                      float* out, ssd_stream_t stream) {
+  g_err[0] = 0;
+  int s = check_dims(batch, seqlen, ngroups, 1, ngroups, k, chunk_size);
+  if (s) return s;
+  if (!a || !b || !out) return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  return cuda_status(ssd::launch_bmm_chunk(a, b, dtype, seq_idx, causal, batch, seqlen, ngroups, k, chunk_size,
+                                           out, (cudaStream_t)stream), "bmm_chunk");
+}
+
+int ssd_chunk_scan_fwd(const float* cb, const void* x, int32_t dtype, const float* dt_out,
+                       const float* dA_cumsum, const void* C, const void* states, int32_t states_dtype,
+                       const float* D, int32_t D_ndim, const void* z, const int32_t* seq_idx, int64_t batch,
+                       int64_t seqlen, int64_t nheads, int64_t headdim, int64_t ngroups, int64_t dstate,
+                       int64_t chunk_size, float* out, float* out_x, ssd_stream_t stream) {
+  g_err[0] = 0;
+  int s = check_dims(batch, seqlen, nheads, headdim, ngroups, dstate, chunk_size);
+  if (s) return s;
+  if (!cb || !x || !dt_out || !dA_cumsum || !C || !states || !out) return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(dtype) || !dtype_ok(states_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (D_ndim < 0 || D_ndim > 2 || (D_ndim && !D)) return fail(SSD_ERR_INVALID_ARG, "bad D_ndim / D");
+  if (out_x && !z) return fail(SSD_ERR_INVALID_ARG, "out_x requires z");
+  return cuda_status(ssd::launch_chunk_scan(cb, x, dtype, dt_out, dA_cumsum, C, states, states_dtype, D, D_ndim,
+                                            z, seq_idx, batch, seqlen, nheads, headdim, ngroups, dstate,
+                                            chunk_size, out, out_x, (cudaStream_t)stream), "chunk_scan");
+}
+
+int ssd_chunk_state_varlen_fwd(const void* B, const void* x, int32_t dtype, const float* dt_out,
+                               const float* dA_cumsum, const int32_t* cu_seqlens, int32_t num_seqs,
+                               const void* chunk_states, int32_t states_dtype, int64_t total_seqlen,
+                               int64_t nheads, int64_t headdim, int64_t ngroups, int64_t dstate,
+                               int64_t chunk_size, float* out, ssd_stream_t stream) {
+  g_err[0] = 0;
+  int s = check_dims(1, total_seqlen, nheads, headdim, ngroups, dstate, chunk_size);
+  if (s) return s;
+  if (num_seqs <= 0) return fail(SSD_ERR_INVALID_ARG, "num_seqs must be positive");
+  if (!B || !x || !dt_out || !dA_cumsum || !cu_seqlens || !chunk_states || !out)
+    return fail(SSD_ERR_INVALID_ARG, "null pointer");
+  if (!dtype_ok(dtype) || !dtype_ok(states_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  return cuda_status(ssd::launch_chunk_state_varlen(B, x, dtype, dt_out, dA_cumsum, cu_seqlens, num_seqs,
+                                                    chunk_states, states_dtype, total_seqlen, nheads, headdim,
+                                                    ngroups, dstate, chunk_size, out, (cudaStream_t)stream),
+                     "chunk_state_varlen");
+}
+
+int ssd_selective_state_update(const ssu_params_t* p, ssd_stream_t stream) {
+  g_err[0] = 0;
+  if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
+  if (p->batch <= 0 || p->nheads <= 0 || p->headdim <= 0 || p->ngroups <= 0 || p->dstate <= 0)
+    return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
+  if (p->nheads % p->ngroups) return fail(SSD_ERR_INVALID_ARG, "nheads must be a multiple of ngroups");
+  if (!dtype_ok(p->dtype) || !dtype_ok(p->dt_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (!p->state || !p->x || !p->dt || !p->A || !p->B || !p->C || !p->out)
+    return fail(SSD_ERR_INVALID_ARG, "state, x, dt, A, B, C and out are required");
+  if (p->dt_ndim != 2 && p->dt_ndim != 3) return fail(SSD_ERR_INVALID_ARG, "dt_ndim must be 2 or 3");
+  if (p->A_ndim != 1 && p->A_ndim != 3) return fail(SSD_ERR_INVALID_ARG, "A_ndim must be 1 or 3");
+  if (p->D_ndim < 0 || p->D_ndim > 2 || (p->D_ndim && !p->D)) return fail(SSD_ERR_INVALID_ARG, "bad D_ndim / D");
+  if (p->dt_bias && (p->dt_bias_ndim < 1 || p->dt_bias_ndim > 2)) return fail(SSD_ERR_INVALID_ARG, "bad dt_bias_ndim");
+  if (p->dstate > 8192) return fail(SSD_ERR_UNSUPPORTED, "dstate > 8192 unsupported");
+  return cuda_status(ssd::launch_ssu(p, (cudaStream_t)stream), "selective_state_update");
+}
+
+}  // extern "C"
