@@ -197,7 +197,7 @@ def cpu_oracle_sample(cfg, budget_s=12.0, heads=None):
     small = S.scaled(cfg, nheads=hs)
     inp = S.make_ssd_inputs(small, 99)
     reps, t_tot = 0, 0.0
-    while t_tot < budget_s and reps < 50:
+    while reps == 0 or (t_tot < budget_s and reps < 50):
         t0 = time.perf_counter()
         R.ssd_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], cfg.chunk_size,
                        D=inp["D"], z=inp["z"], dt_bias=inp["dt_bias"],
