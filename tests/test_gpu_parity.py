@@ -274,7 +274,7 @@ def test_selective_state_update(case, inplace):
     x = S.round_to(f(b, H, P), dtype)
     dt = S.round_to(f(b, H) if dtn == 2 else f(b, H, P), dtype)
     if not sp:
-        dt = np.abs(dt) * 0.1
+        dt = S.round_to(np.abs(dt) * 0.1, dtype)
     A = (-np.abs(f(H)) if An == 1 else -np.abs(f(H, P, N))).astype(np.float32)
     Bm, Cm = S.round_to(f(b, G, N), dtype), S.round_to(f(b, G, N), dtype)
     D = None if Dn == 0 else (f(H) if Dn == 1 else f(H, P))
