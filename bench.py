@@ -334,16 +334,95 @@ def run_ours(args, cfg, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_ssu(args, rank, world, device):
+    """c4: selective_state_update decode steps, state updated in place (1000 steps timed as
+    one region; tokens = batch x steps)."""
+    from mamba2_b200 import _lib
+    from mamba2_b200.ops.selective_state_update import selective_state_update
+    cfg = S.CONFIGS["c4"]
+    hbm, tfl, peak_kind = _peaks()
+    u = S.make_ssu_inputs(cfg, 1004 + rank)
+    tdt = torch.bfloat16
+    st = torch.from_numpy(u["state"]).to(device)
+    d = {k: torch.from_numpy(u[k]).to(device=device, dtype=(tdt if k in ("x", "z", "dt", "B", "C") else torch.float32))
+         for k in ("x", "z", "dt", "B", "C", "A", "D", "dt_bias")}
+    b, H, P, N, G = cfg.batch, cfg.nheads, cfg.headdim, cfg.dstate, cfg.ngroups
+    out = torch.empty((b, H, P), device=device, dtype=torch.float32)
+    p = _lib.SsuParams(batch=b, nheads=H, headdim=P, ngroups=G, dstate=N, dtype=1, dt_dtype=1, dt_ndim=2,
+                       A_ndim=1, D_ndim=1, dt_bias_ndim=1, dt_softplus=1)
+    p.state, p.x, p.dt, p.A = st.data_ptr(), d["x"].data_ptr(), d["dt"].data_ptr(), d["A"].data_ptr()
+    p.B, p.C, p.D, p.z = d["B"].data_ptr(), d["C"].data_ptr(), d["D"].data_ptr(), d["z"].data_ptr()
+    p.dt_bias, p.out = d["dt_bias"].data_ptr(), out.data_ptr()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream()
+    steps = args.steps if args.steps != 50 else cfg.steps
+    g = torch.cuda.CUDAGraph()
+    s2 = torch.cuda.Stream()
+    s2.wait_stream(stream)
+    with torch.cuda.stream(s2):
+        _lib.check(lib.ssd_selective_state_update(p, s2.cuda_stream))
+    stream.wait_stream(s2)
+    with torch.cuda.graph(g):
+        _lib.check(lib.ssd_selective_state_update(p, torch.cuda.current_stream().cuda_stream))
+    for _ in range(max(args.warmup, 3)):
+        g.replay()
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(lambda i: g.replay(), steps, stream)
+    clocks = clk.stop() if clk else None
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    value = steps * b * world / (ms / 1e3)
+    state_bytes = b * H * P * N * 4
+    io = b * H * P * 2 * 2 + b * H * 2 + 2 * b * G * N * 2 + b * H * P * 4
+    step_bytes = 2 * state_bytes + io
+    # e2e: per step H2D of the token inputs, D2H of out; state stays resident (as in decode)
+    host = {k: d[k].cpu().pin_memory() for k in ("x", "z", "dt", "B", "C")}
+    out_h = torch.empty((b, H, P), dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+
+    def e2e_step(_i):
+        dd = {k: host[k].to(device, non_blocking=True) for k in host}
+        _, o = selective_state_update(st, dd["x"], dd["dt"], d["A"], dd["B"], dd["C"], D=d["D"], z=dd["z"],
+                                      dt_bias=d["dt_bias"], dt_softplus=True, inplace=True)
+        out_h.copy_(o, non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    e2e_steps = min(steps, 200)
+    ms_e2e = time_region(e2e_step, e2e_steps, stream)
+    if rank != 0:
+        return
+    ach = step_bytes / (ms / steps / 1e3) / 1e9
+    line = {"metric": "selective_state_update decode tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": cfg.name, "key": "c4", "batch": b, "nheads": H, "headdim": P,
+                       "ngroups": G, "dstate": N, "input_dtype": "bf16", "state": "f32 in place",
+                       "l2": f"state {state_bytes / 1e9:.2f} GB > L2"},
+            "roofline": {"kernel": "ssu_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "peak_kind": peak_kind, "traffic": None},
+            "e2e": {"value": e2e_steps * b * world / (ms_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4},
+            "gpu_launches": steps, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3"])
+    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = S.CONFIGS[args.config]
+    if args.impl == "reference" and args.config == "c4":
+        raise SystemExit("reference arm for c4 not implemented")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
@@ -355,7 +434,10 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=device)
     try:
-        run_ours(args, cfg, rank, world, device)
+        if args.config == "c4":
+            run_ssu(args, rank, world, device)
+        else:
+            run_ours(args, cfg, rank, world, device)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

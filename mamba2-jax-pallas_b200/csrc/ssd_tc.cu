@@ -15,13 +15,14 @@
 //   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM
 //   E1    xs[t][p]  = x[t][p] exp(dA_last - dA_t) dt_t  (chunk-end seq only)  -> smem bf16
 //   MMA_L Lt[n][p]  = B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM
-//   E3    S_{c+1}   = keep_c exp(dA_last) S_c + Lt      (registers, f32)      -> smem bf16
+//   E3    S_{c+1}   = keep_c exp(dA_last) S_c + Lt      (TMEM, f32)           -> smem bf16
 //   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi + D x ; * silu(z)
 // Decay factors are always formed from differences of the in-chunk cumulative sums
 // (never exp(dA_m) * exp(-dA_t)), as ssd_naive.py:264-268 does.
 //
-// Warp roles: warps 0-3 epilogue (thread r owns row r = TMEM lane r), warp 4 TMA
-// producer, warp 5 MMA issuer.  Every mbarrier wait is bounded; on timeout the CTA
+// Warp roles: warps 0-3 build scores and scaled x (chunk row r = TMEM lane r), warps 4-7
+// update the state and write the output (they run one phase behind), warp 8 is the TMA
+// producer, warp 9 issues the MMAs.  The running state lives in TMEM (f32).  Every mbarrier wait is bounded; on timeout the CTA
 // records SSD_ERR_TIMEOUT in the status word, drains its async work and exits.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -36,9 +37,9 @@ namespace {
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
 constexpr int NT_ = 128;      // state dim handled by the kernel
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 320;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_CB = 0, COL_Y = 128, COL_YI = 192, COL_L = 256;
+constexpr uint32_t COL_CB = 0, COL_Y = 128, COL_YI = 192, COL_L = 256, COL_ST = 320;
 
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr uint32_t SZ_C = QI * NT_ * 2;          // 32 KB  (two 64-wide swizzled boxes)
@@ -60,6 +61,9 @@ struct Misc {
   float dt[QI];
   int seq[QI];
   float red[4];
+  float red_o[4];
+  float dA_last_o;
+  int end_seq_o;
   uint32_t tmem_base;
   volatile int abort;
 };
@@ -114,7 +118,7 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 }
 
 // ---------------------------------------------------------------------------
-// producer (warp 4, lane 0): C, B, x tiles of each chunk into a 2-stage ring
+// producer (warp 8, lane 0): C, B, x tiles of each chunk into a 2-stage ring
 // ---------------------------------------------------------------------------
 __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int g) {
   const uint32_t bytes = SZ_STAGE;
@@ -142,7 +146,7 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
 }
 
 // ---------------------------------------------------------------------------
-// MMA issuer (warp 5, lane 0)
+// MMA issuer (warp 9, lane 0)
 // ---------------------------------------------------------------------------
 __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   const uint32_t tmem = m->tmem_base;
@@ -208,57 +212,66 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
 }
 
 // ---------------------------------------------------------------------------
-// epilogue warpgroup (warps 0-3): thread r owns chunk row r and TMEM lane r
+// helpers shared by the two worker warpgroups
 // ---------------------------------------------------------------------------
-__device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
-  const int r = threadIdx.x;          // 0..127
+struct ChunkDt {
+  float raw;
+  int seq;
+};
+
+__device__ __forceinline__ ChunkDt load_dt(const TcArgs& a, int bi, int h, int c, int r) {
+  ChunkDt d{0.f, -1};
+  const int64_t pos = (int64_t)c * QI + r;
+  if (c < a.nci && pos < a.L) {
+    const int64_t di = ((int64_t)bi * a.L + pos) * a.H + h;
+    d.raw = a.dt_bf16 ? __bfloat162float(((const bf16*)a.dt)[di]) : ((const float*)a.dt)[di];
+    d.seq = a.seq_idx ? a.seq_idx[(int64_t)bi * a.L + pos] : 0;
+  }
+  return d;
+}
+
+// 16-byte words of a bf16 row, scaled by `s`, repacked.
+__device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
+  uint4 o;
+  float2 f;
+  f = unpack_bf16(w.x); o.x = pack_bf16(f.x * s, f.y * s);
+  f = unpack_bf16(w.y); o.y = pack_bf16(f.x * s, f.y * s);
+  f = unpack_bf16(w.z); o.z = pack_bf16(f.x * s, f.y * s);
+  f = unpack_bf16(w.w); o.w = pack_bf16(f.x * s, f.y * s);
+  return o;
+}
+
+__device__ __forceinline__ void set_word(uint4 (&o)[4], int w, uint32_t v) {
+  if ((w & 3) == 0) o[w >> 2].x = v;
+  else if ((w & 3) == 1) o[w >> 2].y = v;
+  else if ((w & 3) == 2) o[w >> 2].z = v;
+  else o[w >> 2].w = v;
+}
+
+// ---------------------------------------------------------------------------
+// score worker (warps 0-3): dt/dA of the chunk, xs = x * scale, S = CB o decay
+// ---------------------------------------------------------------------------
+__device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
+  const int r = threadIdx.x;  // 0..127
   const int q = r >> 5, lane = r & 31;
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
-  const int64_t L = a.L, H = a.H;
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  float Dh[PT / 32 > 0 ? 1 : 1];
-  Dh[0] = a.D_ndim == 1 ? a.D[h] : 0.f;
+  // decays factor as exp(dA_r - dA_R) * exp(dA_R - dA_t) with both exponents <= 0 when
+  // the cumulative sum is non-increasing (A <= 0, dt >= 0); otherwise every element is
+  // formed directly.
+  const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
+  const bool has_seq = a.seq_idx != nullptr;
   uint8_t* S_sm = sm + OFF_S;
   uint8_t* xs_sm = sm + OFF_XS;
-  uint8_t* st_sm = sm + OFF_ST;
-
-  // running state, row n = r:  st[p] = S[n=r][p]
-  float st[PT];
-  const int64_t bh = (int64_t)bi * H + h;
-#pragma unroll
-  for (int p = 0; p < PT; ++p) st[p] = a.init ? a.init[(bh * PT + p) * NT_ + r] : 0.f;
-  auto write_state = [&]() {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint4 v;
-      v.x = pack_bf16(st[8 * j + 0], st[8 * j + 1]);
-      v.y = pack_bf16(st[8 * j + 2], st[8 * j + 3]);
-      v.z = pack_bf16(st[8 * j + 4], st[8 * j + 5]);
-      v.w = pack_bf16(st[8 * j + 6], st[8 * j + 7]);
-      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = v;
-    }
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[ST_FULL]);
-  };
-  write_state();
-
-  int prev_end = 0;
+  ChunkDt nxt = load_dt(a, bi, h, 0, r);
   for (int c = 0; c < a.nci; ++c) {
     const int s = c & 1;
     const int64_t t0 = (int64_t)c * QI;
-    const int64_t pos = t0 + r;
-    const bool valid = pos < L;
-    // ---- E0: dt processing and in-chunk cumulative sum of dt*A ----------------
-    float dtv = 0.f;
-    int seqv = a.seq_idx ? -1 : 0;
-    if (valid) {
-      const int64_t di = ((int64_t)bi * L + pos) * H + h;
-      const float raw = a.dt_bf16 ? __bfloat162float(((const bf16*)a.dt)[di]) : ((const float*)a.dt)[di];
-      dtv = dt_process(raw, bias, a.softplus, a.lo, a.hi);
-      if (a.seq_idx) seqv = a.seq_idx[(int64_t)bi * L + pos];
-    }
+    const ChunkDt cur = nxt;
+    nxt = load_dt(a, bi, h, c + 1, r);
+    const float dtv = (t0 + r < a.L) ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    const int seqv = cur.seq;
     float cs = warp_incl_scan(dtv * Ah);
     if (lane == 31) m->red[q] = cs;
     ptx::named_bar_sync(1, 128);
@@ -269,29 +282,18 @@ __device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
     m->seq[r] = seqv;
     ptx::named_bar_sync(1, 128);
     const float dA_last = m->dA[QI - 1];
-    const int last_valid = (int)min((int64_t)QI - 1, L - 1 - t0);
+    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
     const int end_seq = m->seq[last_valid];
-    const int prev_seq = (!a.seq_idx || c == 0) ? 0 : a.seq_idx[(int64_t)bi * L + t0 - 1];
-    const bool keep = end_seq == prev_end;
-    prev_end = end_seq;
     const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(dA_last - dA) * dtv : 0.f;
-    const float sdec = (seqv == prev_seq) ? __expf(dA) : 0.f;
-    const float chunk_decay = keep ? __expf(dA_last) : 0.f;
 
-    // ---- E1: xs = x * scale  (x row kept packed in registers for the D term) ----
+    // ---- E1: xs = x * scale ------------------------------------------------------
     if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
+    if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
     const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-    uint4 xr[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      xr[j] = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
-      uint4 o;
-      float2 f;
-      f = unpack_bf16(xr[j].x); o.x = pack_bf16(f.x * scale, f.y * scale);
-      f = unpack_bf16(xr[j].y); o.y = pack_bf16(f.x * scale, f.y * scale);
-      f = unpack_bf16(xr[j].z); o.z = pack_bf16(f.x * scale, f.y * scale);
-      f = unpack_bf16(xr[j].w); o.w = pack_bf16(f.x * scale, f.y * scale);
-      *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, j)) = o;
+      const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
+      *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, j)) = scale_row16(w, scale);
     }
     ptx::fence_proxy_async_smem();
     __syncwarp();
@@ -300,28 +302,44 @@ __device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
       ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
     }
 
-    // ---- E2: scores S[r][t] = CB * exp(dA_r - dA_t) * dt_t, causal, same sequence ----
+    // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
     if (!wait_bar(m, B_CB, c & 1, a.status)) return;
+    if (c > 0 && !wait_bar(m, B_Y, (c - 1) & 1, a.status)) return;   // MMA2(c-1) done with S
     ptx::tc_fence_after();
+    const float dA_R = m->dA[q * 32];
+    const float u = __expf(dA - dA_R);
 #pragma unroll 1
     for (int k32 = 0; k32 < 4; ++k32) {
       uint4 o[4];
-      if (k32 <= q) {
+      if (k32 < q && factor) {
+        const int tl = k32 * 32 + lane;
+        const float vl = __expf(dA_R - m->dA[tl]) * m->dt[tl];
+        const int sl = m->seq[tl];
+        float v[32];
+        ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float s0 = v[i] * u * __shfl_sync(0xffffffffu, vl, i);
+          float s1 = v[i + 1] * u * __shfl_sync(0xffffffffu, vl, i + 1);
+          if (has_seq) {
+            if (__shfl_sync(0xffffffffu, sl, i) != seqv) s0 = 0.f;
+            if (__shfl_sync(0xffffffffu, sl, i + 1) != seqv) s1 = 0.f;
+          }
+          set_word(o, i >> 1, pack_bf16(s0, s1));
+        }
+      } else if (k32 <= q) {
         float v[32];
         ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);
         ptx::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int t = k32 * 32 + i;
-          float s0 = 0.f, s1 = 0.f;
-          if (t <= r && m->seq[t] == seqv) s0 = v[i] * __expf(dA - m->dA[t]) * m->dt[t];
-          if (t + 1 <= r && m->seq[t + 1] == seqv) s1 = v[i + 1] * __expf(dA - m->dA[t + 1]) * m->dt[t + 1];
-          const uint32_t pk = pack_bf16(s0, s1);
-          const int w = i >> 1;  // 0..15 words
-          if ((w & 3) == 0) o[w >> 2].x = pk;
-          else if ((w & 3) == 1) o[w >> 2].y = pk;
-          else if ((w & 3) == 2) o[w >> 2].z = pk;
-          else o[w >> 2].w = pk;
+          const bool ok0 = t <= r && (!has_seq || m->seq[t] == seqv);
+          const bool ok1 = t + 1 <= r && (!has_seq || m->seq[t + 1] == seqv);
+          const float s0 = ok0 ? v[i] * __expf(dA - m->dA[t]) * m->dt[t] : 0.f;
+          const float s1 = ok1 ? v[i + 1] * __expf(dA - m->dA[t + 1]) * m->dt[t + 1] : 0.f;
+          set_word(o, i >> 1, pack_bf16(s0, s1));
         }
       } else {
 #pragma unroll
@@ -339,65 +357,151 @@ __device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
       ptx::mbar_arrive(&m->bar[CB_FREE]);
       ptx::mbar_arrive(&m->bar[S_FULL]);
     }
+  }
+}
 
-    // ---- E3: state update S_{c+1} = keep * exp(dA_last) * S_c + Lt ----------------
+// ---------------------------------------------------------------------------
+// output worker (warps 4-7): state update in TMEM and the output epilogue
+// ---------------------------------------------------------------------------
+__device__ void out_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
+  const int r = threadIdx.x - 128;  // 0..127
+  const int q = r >> 5, lane = r & 31;
+  const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
+  const int64_t L = a.L, H = a.H;
+  const float Ah = a.A[h];
+  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
+  const float D1 = a.D_ndim == 1 ? a.D[h] : 0.f;
+  uint8_t* st_sm = sm + OFF_ST;
+  const int64_t bh = (int64_t)bi * H + h;
+
+  // state row n = r as bf16 into the MMA3 operand buffer ([n][p], 128B swizzled rows)
+  auto publish_state = [&](const float (&lo)[32], const float (&hi)[32]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float* v = j < 4 ? lo + 8 * j : hi + 8 * (j - 4);
+      uint4 w;
+      w.x = pack_bf16(v[0], v[1]);
+      w.y = pack_bf16(v[2], v[3]);
+      w.z = pack_bf16(v[4], v[5]);
+      w.w = pack_bf16(v[6], v[7]);
+      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = w;
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&m->bar[ST_FULL]);
+  };
+  {
+    float lo[32], hi[32];
+#pragma unroll
+    for (int p = 0; p < 32; ++p) {
+      lo[p] = a.init ? a.init[(bh * PT + p) * NT_ + r] : 0.f;
+      hi[p] = a.init ? a.init[(bh * PT + 32 + p) * NT_ + r] : 0.f;
+    }
+    ptx::tmem_st32(tmem + COL_ST, lo);
+    ptx::tmem_st32(tmem + COL_ST + 32, hi);
+    ptx::tmem_st_wait();
+    publish_state(lo, hi);
+  }
+
+  int prev_end = 0;
+  ChunkDt nxt = load_dt(a, bi, h, 0, r);
+  for (int c = 0; c < a.nci; ++c) {
+    const int s = c & 1;
+    const int64_t t0 = (int64_t)c * QI;
+    const int64_t pos = t0 + r;
+    const bool valid = pos < L;
+    const int64_t o0 = (((int64_t)bi * L + (valid ? pos : 0)) * H + h) * PT;
+    // z row of this chunk: issued now, used at the end of the chunk
+    uint4 zr[8];
+    if (a.z && valid) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) zr[j] = __ldg(reinterpret_cast<const uint4*>(a.z + o0) + j);
+    }
+    const ChunkDt cur = nxt;
+    nxt = load_dt(a, bi, h, c + 1, r);
+    const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    float cs = warp_incl_scan(dtv * Ah);
+    if (lane == 31) m->red_o[q] = cs;
+    const int last_valid = (int)min((int64_t)QI - 1, L - 1 - t0);
+    if (r == last_valid) m->end_seq_o = cur.seq;
+    ptx::named_bar_sync(2, 128);
+    for (int w = 0; w < q; ++w) cs += m->red_o[w];
+    const float dA = cs;
+    const float dA_last = m->red_o[0] + m->red_o[1] + m->red_o[2] + m->red_o[3];
+    const int end_seq = m->end_seq_o;
+    ptx::named_bar_sync(2, 128);
+    const bool keep = end_seq == prev_end;
+    const float sdec = (cur.seq == prev_end) ? __expf(dA) : 0.f;   // prev chunk's end seq
+    prev_end = end_seq;
+    const float decay = keep ? __expf(dA_last) : 0.f;
+
+    // x row for the D term (copied out so the stage can be recycled)
+    if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
+    uint4 xr[8];
+    const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[j] = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+
+    // ---- E3: S_{c+1} = decay * S_c + Lt  (TMEM), bf16 copy for the next MMA3 ----------
     if (!wait_bar(m, B_L, c & 1, a.status)) return;
     ptx::tc_fence_after();
-    {
-      float v[32];
-      ptx::tmem_ld32(tmem + COL_L, v);
-      ptx::tmem_ld_wait();
+    float lo[32], hi[32], v[32];
+    ptx::tmem_ld32(tmem + COL_L, v);
+    ptx::tmem_ld32(tmem + COL_ST, lo);
+    ptx::tmem_ld_wait();
 #pragma unroll
-      for (int p = 0; p < 32; ++p) st[p] = chunk_decay * st[p] + v[p];
-      ptx::tmem_ld32(tmem + COL_L + 32, v);
-      ptx::tmem_ld_wait();
+    for (int p = 0; p < 32; ++p) lo[p] = decay * lo[p] + v[p];
+    ptx::tmem_ld32(tmem + COL_L + 32, v);
+    ptx::tmem_ld32(tmem + COL_ST + 32, hi);
+    ptx::tmem_ld_wait();
 #pragma unroll
-      for (int p = 0; p < 32; ++p) st[32 + p] = chunk_decay * st[32 + p] + v[p];
-    }
+    for (int p = 0; p < 32; ++p) hi[p] = decay * hi[p] + v[p];
+    ptx::tmem_st32(tmem + COL_ST, lo);
+    ptx::tmem_st32(tmem + COL_ST + 32, hi);
+    ptx::tmem_st_wait();
     ptx::tc_fence_before();
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&m->bar[L_FREE]);
-    if (!wait_bar(m, B_YI, c & 1, a.status)) return;   // MMA3 finished reading S_c
-    if (c + 1 < a.nci) write_state();
+    if (!wait_bar(m, B_YI, c & 1, a.status)) return;   // MMA3(c) done reading S_c
+    if (c + 1 < a.nci) publish_state(lo, hi);
+    if (c + 1 == a.nci && a.final_states) {
+#pragma unroll
+      for (int p = 0; p < 32; ++p) {
+        a.final_states[(bh * PT + p) * NT_ + r] = lo[p];
+        a.final_states[(bh * PT + 32 + p) * NT_ + r] = hi[p];
+      }
+    }
 
-    // ---- E4: out = Y + sdec * Yi + D x, z gate --------------------------------------
+    // ---- E4: out = Y + sdec * Yi + D x; z gate ------------------------------------------
     if (!wait_bar(m, B_Y, c & 1, a.status)) return;
     ptx::tc_fence_after();
-    float y[PT];
-    {
-      float v[32];
-      ptx::tmem_ld32(tmem + COL_Y, v);
-      ptx::tmem_ld_wait();
 #pragma unroll
-      for (int p = 0; p < 32; ++p) y[p] = v[p];
-      ptx::tmem_ld32(tmem + COL_Y + 32, v);
-      ptx::tmem_ld_wait();
-#pragma unroll
-      for (int p = 0; p < 32; ++p) y[32 + p] = v[p];
-      ptx::tmem_ld32(tmem + COL_YI, v);
+    for (int half = 0; half < 2; ++half) {
+      float y[32];
+      ptx::tmem_ld32(tmem + COL_Y + 32 * half, y);
+      ptx::tmem_ld32(tmem + COL_YI + 32 * half, v);
       ptx::tmem_ld_wait();
 #pragma unroll
       for (int p = 0; p < 32; ++p) y[p] += sdec * v[p];
-      ptx::tmem_ld32(tmem + COL_YI + 32, v);
-      ptx::tmem_ld_wait();
-#pragma unroll
-      for (int p = 0; p < 32; ++p) y[32 + p] += sdec * v[p];
-    }
-    ptx::tc_fence_before();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[Y_FREE]);
-    if (valid) {
-      const int64_t o0 = (((int64_t)bi * L + pos) * H + h) * PT;
+      if (half == 1) {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&m->bar[Y_FREE]);
+      }
+      if (!valid) continue;
       if (a.D_ndim) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t wv[4] = {xr[j].x, xr[j].y, xr[j].z, xr[j].w};
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w4 = xr[4 * half + j];
+          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float2 f = unpack_bf16(wv[k]);
             const int p = 8 * j + 2 * k;
-            const float d0 = a.D_ndim == 1 ? Dh[0] : a.D[(int64_t)h * PT + p];
-            const float d1 = a.D_ndim == 1 ? Dh[0] : a.D[(int64_t)h * PT + p + 1];
+            const float d0 = a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + 32 * half + p];
+            const float d1 = a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + 32 * half + p + 1];
             y[p] += d0 * f.x;
             y[p + 1] += d1 * f.y;
           }
@@ -406,14 +510,13 @@ __device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
       if (a.z) {
         if (a.out_x) {
 #pragma unroll
-          for (int p = 0; p < PT; p += 4)
-            *reinterpret_cast<float4*>(a.out_x + o0 + p) = make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]);
+          for (int p = 0; p < 32; p += 4)
+            *reinterpret_cast<float4*>(a.out_x + o0 + 32 * half + p) = make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]);
         }
-        const uint4* zp = reinterpret_cast<const uint4*>(a.z + o0);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 zz = __ldg(zp + j);
-          const uint32_t wv[4] = {zz.x, zz.y, zz.z, zz.w};
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w4 = zr[4 * half + j];
+          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float2 f = unpack_bf16(wv[k]);
@@ -423,13 +526,9 @@ __device__ void epilogue(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
         }
       }
 #pragma unroll
-      for (int p = 0; p < PT; p += 4)
-        __stcs(reinterpret_cast<float4*>(a.out + o0 + p), make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]));
+      for (int p = 0; p < 32; p += 4)
+        __stcs(reinterpret_cast<float4*>(a.out + o0 + 32 * half + p), make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]));
     }
-  }
-  if (a.final_states) {
-#pragma unroll
-    for (int p = 0; p < PT; ++p) a.final_states[(bh * PT + p) * NT_ + r] = st[p];
   }
 }
 
@@ -445,8 +544,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   if (threadIdx.x == 0) {
     ptx::mbar_init(&m->bar[FULL0], 1);
     ptx::mbar_init(&m->bar[FULL1], 1);
-    ptx::mbar_init(&m->bar[EMPTY0], 5);   // MMA commit + 4 epilogue warps
-    ptx::mbar_init(&m->bar[EMPTY1], 5);
+    ptx::mbar_init(&m->bar[EMPTY0], 9);   // MMA commit + 4 score warps + 4 output warps
+    ptx::mbar_init(&m->bar[EMPTY1], 9);
     ptx::mbar_init(&m->bar[B_CB], 1);
     ptx::mbar_init(&m->bar[CB_FREE], 4);
     ptx::mbar_init(&m->bar[B_YI], 1);
@@ -461,12 +560,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     m->abort = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     ptx::prefetch_tmap(&a.tm_x);
     ptx::prefetch_tmap(&a.tm_b);
     ptx::prefetch_tmap(&a.tm_c);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     ptx::tmem_alloc(&m->tmem_base, TMEM_COLS);
     ptx::tmem_relinquish();
   }
@@ -475,15 +574,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   ptx::tc_fence_after();
 
   if (warp < 4) {
-    epilogue(a, sm, m, bi, h);
-  } else if (warp == 4) {
+    score_worker(a, sm, m, bi, h);
+  } else if (warp < 8) {
+    out_worker(a, sm, m, bi, h);
+  } else if (warp == 8) {
     if (lane == 0) producer(a, sm, m, bi, h, g);
   } else {
     if (lane == 0) mma_issuer(a, sm, m);
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(m->tmem_base, TMEM_COLS);
   }

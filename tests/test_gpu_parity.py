@@ -312,3 +312,18 @@ def test_ssu_decode_loop_matches_prefill():
         outs.append(o)
     assert rel_l2(state, final.double().cpu().numpy()) <= 1e-5
     assert rel_l2(torch.stack(outs, 1), out.double().cpu().numpy()) <= 1e-5
+
+
+def test_tensor_core_path_selected():
+    """bf16, P=64, N=128 runs the fused tcgen05 kernel (one launch); fp32 does not."""
+    from mamba2_b200.runner import SsdForward
+    for dtype, want in (("bf16", True), ("f32", False)):
+        cfg = S.SsdConfig("t", 1, 256, 4, 64, 2, 128, 128, dtype)
+        d = dev_inputs(S.make_ssd_inputs(cfg, 1), dtype)
+        r = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 128, dt_bias=d["dt_bias"], dt_softplus=True)
+        assert r.uses_tc == want
+        assert r.launches_per_step == (1 if want else 5)
+        r()
+        torch.cuda.synchronize()
+        if want:
+            assert int(r.workspace[:4].view(torch.int32).item()) == 0  # device status word
