@@ -1,7 +1,6 @@
 // Fused tcgen05 SSD forward for bf16 inputs (sm_100a).
 //
-// One CTA owns one (batch, head) and walks the sequence in internal chunks of 128
-// tokens, carrying the running state S (N x P, f32) in the epilogue threads' registers.
+// One CTA owns one (batch, head) and walks the sequence in internal chunks of 128 tokens.
 // Nothing but the inputs, the outputs and the final state touches HBM: no chunk states,
 // no CB matrix, no dA arrays.  The result does not depend on the internal chunk size
 // (the reference's chunk_size only sets its own tiling; the seq_idx rules of
@@ -11,19 +10,26 @@
 // Per chunk c (t = token in chunk, m = output row, n = state dim, p = head dim):
 //   MMA1  CB[m][t]  = C[m][:] . B[t][:]                 (M=128, N=128, K=N)   TMEM
 //   E2    S[m][t]   = CB[m][t] exp(dA_m - dA_t) dt_t    (t <= m, same seq)    -> smem bf16
-//   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM
-//   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM
+//   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM (2 bufs)
+//   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM (2 bufs)
 //   E1    xs[t][p]  = x[t][p] exp(dA_last - dA_t) dt_t  (chunk-end seq only)  -> smem bf16
-//   MMA_L Lt[n][p]  = B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM
-//   E3    S_{c+1}   = keep_c exp(dA_last) S_c + Lt      (TMEM, f32)           -> smem bf16
+//   MMA_L St[n][p] += B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM state
+//   E3    S_{c+1}   = St (already keep_c exp(dA_last_c) S_c + L_c);  bf16 -> smem for MMA3,
+//                     St <- keep_{c+1} exp(dA_last_{c+1}) S_{c+1} for the next MMA_L
 //   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi + D x ; * silu(z)
 // Decay factors are always formed from differences of the in-chunk cumulative sums
 // (never exp(dA_m) * exp(-dA_t)), as ssd_naive.py:264-268 does.
 //
-// Warp roles: warps 0-3 build scores and scaled x (chunk row r = TMEM lane r), warps 4-7
-// update the state and write the output (they run one phase behind), warp 8 is the TMA
-// producer, warp 9 issues the MMAs.  The running state lives in TMEM (f32).  Every mbarrier wait is bounded; on timeout the CTA
-// records SSD_ERR_TIMEOUT in the status word, drains its async work and exits.
+// The only serial dependence between chunks is the state: E3(c) -> MMA3/MMA_L(c+1) ->
+// E3(c+1).  Everything else is pipelined around it by warp role:
+//   warps 0-3  (S0) dt/dA of the chunk, half of xs and of the score blocks
+//   warps 4-7  (S1) the other halves
+//   warps 8-11 (T)  state recurrence E3
+//   warps 12-15(O)  output epilogue E4 (one chunk behind, double-buffered Y/Yi)
+//   warp 16 TMA producer, warp 17 MMA issuer.
+// Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk rows of its quadrant.
+// Every mbarrier wait is bounded; on timeout the CTA records SSD_ERR_TIMEOUT in the status
+// word, drains its async work and exits.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -37,9 +43,9 @@ namespace {
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
 constexpr int NT_ = 128;      // state dim handled by the kernel
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 576;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_CB = 0, COL_Y = 128, COL_YI = 192, COL_L = 256, COL_ST = 320;
+constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192, COL_ST = 384;  // Y/Yi buffer b at +128*b
 
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr uint32_t SZ_C = QI * NT_ * 2;          // 32 KB  (two 64-wide swizzled boxes)
@@ -50,24 +56,29 @@ constexpr uint32_t OFF_S = 2 * SZ_STAGE;         // scores, 32 KB (two K-blocks)
 constexpr uint32_t OFF_XS = OFF_S + QI * QI * 2; // 16 KB
 constexpr uint32_t OFF_ST = OFF_XS + SZ_X;       // state bf16 [n][p], 16 KB
 constexpr uint32_t OFF_MISC = OFF_ST + NT_ * PT * 2;
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 2048 + 1024;
+constexpr uint32_t MISC_BYTES = 2560;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;   // bytes used from the 1024-aligned base
+constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
 
-enum Bar { FULL0, FULL1, EMPTY0, EMPTY1, B_CB, CB_FREE, B_YI, ST_FULL, XS_FULL, B_L, L_FREE, S_FULL, B_Y, Y_FREE,
-           DRAIN, NBARS };
+enum Bar { FULL0, FULL1, EMPTY0, EMPTY1, B_CB, CB_FREE, XS_FULL, S_FULL, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0,
+           Y_FREE1, DRAIN, NBARS };
+
+// arrivals per phase
+constexpr uint32_t EMPTY_COUNT = 1 + 8 + 4;   // MMA commit, S0+S1 warps (xs), O warps (D x)
 
 struct Misc {
   uint64_t bar[NBARS];
-  float dA[QI];
-  float dt[QI];
-  int seq[QI];
-  float red[4];
-  float red_o[4];
-  float dA_last_o;
-  int end_seq_o;
+  float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
+  float dt[2][QI];      // processed dt
+  float red_s[4];
+  float red_t[2][4];
+  int end_t[2];
+  float red_o[2][4];
+  int end_o[2];
   uint32_t tmem_base;
   volatile int abort;
 };
-static_assert(sizeof(Misc) <= 2048, "misc area");
+static_assert(sizeof(Misc) <= MISC_BYTES, "misc area");
 
 struct TcArgs {
   CUtensorMap tm_x, tm_b, tm_c;
@@ -118,7 +129,7 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 }
 
 // ---------------------------------------------------------------------------
-// producer (warp 8, lane 0): C, B, x tiles of each chunk into a 2-stage ring
+// producer (warp 16, lane 0): C, B, x tiles of each chunk into a 2-stage ring
 // ---------------------------------------------------------------------------
 __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int g) {
   const uint32_t bytes = SZ_STAGE;
@@ -146,7 +157,7 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
 }
 
 // ---------------------------------------------------------------------------
-// MMA issuer (warp 9, lane 0)
+// MMA issuer (warp 17, lane 0)
 // ---------------------------------------------------------------------------
 __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   const uint32_t tmem = m->tmem_base;
@@ -155,14 +166,13 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   constexpr uint32_t ID_YI = ptx::idesc_bf16_f32(128, 64, 0, 1);
   constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
   constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
-  bool ok = true;
-  for (int c = 0; c < a.nci && ok; ++c) {
-    const int s = c & 1;
+  for (int c = 0; c < a.nci; ++c) {
+    const int s = c & 1, yb = c & 1;
     const uint32_t st = base + OFF_STAGE + s * SZ_STAGE;
     const uint32_t sC = st, sB = st + SZ_C, sX = st + 2 * SZ_C;
     // MMA1: CB = C . B^T (both K-major: row = token, K = state dim in two 64-wide boxes)
-    if (!(ok = wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status))) break;
-    if (c > 0 && !(ok = wait_bar(m, CB_FREE, (c - 1) & 1, a.status))) break;
+    if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) break;
+    if (c > 0 && !wait_bar(m, CB_FREE, (c - 1) & 1, a.status)) break;
     ptx::tc_fence_after();
 #pragma unroll
     for (int i = 0; i < NT_ / 16; ++i) {
@@ -171,37 +181,35 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
                    ID_CB, i > 0);
     }
     ptx::mma_commit(&m->bar[B_CB]);
-    // MMA3: Yi = C . S_c^T   (B operand = state [n][p], MN-major)
-    if (!(ok = wait_bar(m, ST_FULL, c & 1, a.status))) break;
-    if (c > 0 && !(ok = wait_bar(m, Y_FREE, (c - 1) & 1, a.status))) break;
+    // MMA3: Yi[yb] = C . S_c^T   (B operand = bf16 state [n][p], MN-major)
+    if (!wait_bar(m, ST_READY, c & 1, a.status)) break;
+    if (c >= 2 && !wait_bar(m, Y_FREE0 + yb, ((c - 2) >> 1) & 1, a.status)) break;
     ptx::tc_fence_after();
 #pragma unroll
     for (int i = 0; i < NT_ / 16; ++i) {
       const uint32_t offa = (i >> 2) * (SZ_C / 2) + (i & 3) * 32;
-      ptx::mma_f16(tmem + COL_YI, ptx::sdesc_sw128(sC + offa, 16, 1024),
+      ptx::mma_f16(tmem + COL_YI0 + 128 * yb, ptx::sdesc_sw128(sC + offa, 16, 1024),
                    ptx::sdesc_sw128(base + OFF_ST + i * 2048, 8192, 1024), ID_YI, i > 0);
     }
-    ptx::mma_commit(&m->bar[B_YI]);
-    // MMA_L: Lt = B^T . xs   (A = B tile read MN-major, B = xs [t][p] MN-major)
-    if (!(ok = wait_bar(m, XS_FULL, c & 1, a.status))) break;
-    if (c > 0 && !(ok = wait_bar(m, L_FREE, (c - 1) & 1, a.status))) break;
+    // MMA_L: St += B^T . xs  onto the pre-scaled state (A = B tile MN-major, B = xs MN-major)
+    if (!wait_bar(m, XS_FULL, c & 1, a.status)) break;
     ptx::tc_fence_after();
 #pragma unroll
     for (int i = 0; i < QI / 16; ++i) {
-      ptx::mma_f16(tmem + COL_L, ptx::sdesc_sw128(sB + i * 2048, SZ_C / 2, 1024),
-                   ptx::sdesc_sw128(base + OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
+      ptx::mma_f16(tmem + COL_ST, ptx::sdesc_sw128(sB + i * 2048, SZ_C / 2, 1024),
+                   ptx::sdesc_sw128(base + OFF_XS + i * 2048, 8192, 1024), ID_L, 1);
     }
-    ptx::mma_commit(&m->bar[B_L]);
-    // MMA2: Y = S . x   (A = scores K-major, B = x [t][p] MN-major)
-    if (!(ok = wait_bar(m, S_FULL, c & 1, a.status))) break;
+    ptx::mma_commit(&m->bar[B_L]);   // state S_{c+1} complete; MMA3(c) done with the bf16 state
+    // MMA2: Y[yb] = S . x   (A = scores K-major, B = x [t][p] MN-major)
+    if (!wait_bar(m, S_FULL, c & 1, a.status)) break;
     ptx::tc_fence_after();
 #pragma unroll
     for (int i = 0; i < QI / 16; ++i) {
       const uint32_t offa = (i >> 2) * (QI * 128) + (i & 3) * 32;
-      ptx::mma_f16(tmem + COL_Y, ptx::sdesc_sw128(base + OFF_S + offa, 16, 1024),
+      ptx::mma_f16(tmem + COL_Y0 + 128 * yb, ptx::sdesc_sw128(base + OFF_S + offa, 16, 1024),
                    ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
     }
-    ptx::mma_commit(&m->bar[B_Y]);
+    ptx::mma_commit(&m->bar[B_Y0 + yb]);
     ptx::mma_commit(&m->bar[EMPTY0 + s]);
   }
   // drain: wait (bounded) until every issued MMA has completed
@@ -212,13 +220,14 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
 }
 
 // ---------------------------------------------------------------------------
-// helpers shared by the two worker warpgroups
+// helpers shared by the worker warpgroups
 // ---------------------------------------------------------------------------
 struct ChunkDt {
   float raw;
   int seq;
 };
 
+// Raw dt and seq id of chunk row r (seq -1 past the end of the sequence or the chunks).
 __device__ __forceinline__ ChunkDt load_dt(const TcArgs& a, int bi, int h, int c, int r) {
   ChunkDt d{0.f, -1};
   const int64_t pos = (int64_t)c * QI + r;
@@ -230,7 +239,24 @@ __device__ __forceinline__ ChunkDt load_dt(const TcArgs& a, int bi, int h, int c
   return d;
 }
 
-// 16-byte words of a bf16 row, scaled by `s`, repacked.
+__device__ __forceinline__ int seq_at(const TcArgs& a, int bi, int64_t pos) {
+  return (pos < a.L) ? a.seq_idx[(int64_t)bi * a.L + pos] : -1;
+}
+
+// Chunk-level values every role needs: dA_last (sum of dt*A over the chunk) and the seq id
+// at the chunk's last valid position.  One reduction through `red`/`endv` + one named
+// barrier; the caller double-buffers the slots by chunk parity.
+__device__ __forceinline__ void chunk_totals(float v, int seqv, int r, int last_valid, float* red, int* endv,
+                                             int bar_id, float& total, int& end_seq) {
+  const float w = warp_sum(v);
+  if ((r & 31) == 0) red[r >> 5] = w;
+  if (r == last_valid) *endv = seqv;
+  ptx::named_bar_sync(bar_id, 128);
+  total = red[0] + red[1] + red[2] + red[3];
+  end_seq = *endv;
+}
+
+// 16-byte word of 8 bf16, scaled by `s`, repacked.
 __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
   uint4 o;
   float2 f;
@@ -241,57 +267,68 @@ __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
   return o;
 }
 
-__device__ __forceinline__ void set_word(uint4 (&o)[4], int w, uint32_t v) {
-  if ((w & 3) == 0) o[w >> 2].x = v;
-  else if ((w & 3) == 1) o[w >> 2].y = v;
-  else if ((w & 3) == 2) o[w >> 2].z = v;
-  else o[w >> 2].w = v;
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
 }
 
 // ---------------------------------------------------------------------------
-// score worker (warps 0-3): dt/dA of the chunk, xs = x * scale, S = CB o decay
+// score workers S0 (warps 0-3, half 0) and S1 (warps 4-7, half 1).
+// S0 computes the chunk's processed dt and cumulative dA into shared memory; both
+// halves then build xs columns [32*half, 32*half+32) and score column blocks
+// {half, half+2} of their rows, which balances the causal triangle (quadrant q has
+// q+1 non-zero 32-column blocks) to at most two blocks per warp.
+// Loops stay rolled (8-column steps) to keep the per-chunk code small.
 // ---------------------------------------------------------------------------
-__device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
-  const int r = threadIdx.x;  // 0..127
+__device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int half) {
+  const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  // decays factor as exp(dA_r - dA_R) * exp(dA_R - dA_t) with both exponents <= 0 when
-  // the cumulative sum is non-increasing (A <= 0, dt >= 0); otherwise every element is
-  // formed directly.
+  // Below the diagonal block the decay factors as exp(dA_r - dA_R) * exp(dA_R - dA_t)
+  // (R = first row of the warp's block) with both exponents <= 0 when the cumulative
+  // sum is non-increasing (A <= 0, dt >= 0); otherwise every element is formed directly.
   const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
   const bool has_seq = a.seq_idx != nullptr;
   uint8_t* S_sm = sm + OFF_S;
   uint8_t* xs_sm = sm + OFF_XS;
-  ChunkDt nxt = load_dt(a, bi, h, 0, r);
+  ChunkDt nxt = half == 0 ? load_dt(a, bi, h, 0, r) : ChunkDt{0.f, 0};
+#pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
-    const int s = c & 1;
+    const int s = c & 1, buf = c & 1;
     const int64_t t0 = (int64_t)c * QI;
-    const ChunkDt cur = nxt;
-    nxt = load_dt(a, bi, h, c + 1, r);
-    const float dtv = (t0 + r < a.L) ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-    const int seqv = cur.seq;
-    float cs = warp_incl_scan(dtv * Ah);
-    if (lane == 31) m->red[q] = cs;
-    ptx::named_bar_sync(1, 128);
-    for (int w = 0; w < q; ++w) cs += m->red[w];
-    const float dA = cs;
-    m->dA[r] = dA;
-    m->dt[r] = dtv;
-    m->seq[r] = seqv;
-    ptx::named_bar_sync(1, 128);
-    const float dA_last = m->dA[QI - 1];
+    const bool valid = t0 + r < a.L;
+    if (half == 0) {
+      const ChunkDt cur = nxt;
+      nxt = load_dt(a, bi, h, c + 1, r);
+      const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+      float cs = warp_incl_scan(dtv * Ah);
+      if (lane == 31) m->red_s[q] = cs;
+      ptx::named_bar_sync(1, 128);
+      for (int w = 0; w < q; ++w) cs += m->red_s[w];
+      m->dA[buf][r] = cs;
+      m->dt[buf][r] = dtv;
+    }
+    ptx::named_bar_sync(3, 256);
+    const float dA = m->dA[buf][r];
+    const float dtv = m->dt[buf][r];
+    const float dA_last = m->dA[buf][QI - 1];
     const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
-    const int end_seq = m->seq[last_valid];
+    int seqv = valid ? 0 : -1, end_seq = 0, sl0 = 0, sl1 = 0;
+    if (has_seq) {
+      seqv = seq_at(a, bi, t0 + r);
+      end_seq = seq_at(a, bi, t0 + last_valid);
+      sl0 = seq_at(a, bi, t0 + half * 32 + lane);
+      sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
+    }
     const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(dA_last - dA) * dtv : 0.f;
 
-    // ---- E1: xs = x * scale ------------------------------------------------------
+    // ---- E1: xs = x * scale (this half's 4 16-byte words of row r) -----------------
     if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
     if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
     const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
+#pragma unroll 1
+    for (int j = 4 * half; j < 4 * half + 4; ++j) {
       const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
       *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, j)) = scale_row16(w, scale);
     }
@@ -304,51 +341,54 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
 
     // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
     if (!wait_bar(m, B_CB, c & 1, a.status)) return;
-    if (c > 0 && !wait_bar(m, B_Y, (c - 1) & 1, a.status)) return;   // MMA2(c-1) done with S
+    if (c > 0 && !wait_bar(m, B_Y0 + ((c - 1) & 1), ((c - 1) >> 1) & 1, a.status)) return;  // MMA2(c-1) done with S
     ptx::tc_fence_after();
-    const float dA_R = m->dA[q * 32];
+    const float dA_R = m->dA[buf][q * 32];
     const float u = __expf(dA - dA_R);
 #pragma unroll 1
-    for (int k32 = 0; k32 < 4; ++k32) {
-      uint4 o[4];
-      if (k32 < q && factor) {
-        const int tl = k32 * 32 + lane;
-        const float vl = __expf(dA_R - m->dA[tl]) * m->dt[tl];
-        const int sl = m->seq[tl];
-        float v[32];
-        ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float s0 = v[i] * u * __shfl_sync(0xffffffffu, vl, i);
-          float s1 = v[i + 1] * u * __shfl_sync(0xffffffffu, vl, i + 1);
-          if (has_seq) {
-            if (__shfl_sync(0xffffffffu, sl, i) != seqv) s0 = 0.f;
-            if (__shfl_sync(0xffffffffu, sl, i + 1) != seqv) s1 = 0.f;
-          }
-          set_word(o, i >> 1, pack_bf16(s0, s1));
-        }
-      } else if (k32 <= q) {
-        float v[32];
-        ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int t = k32 * 32 + i;
-          const bool ok0 = t <= r && (!has_seq || m->seq[t] == seqv);
-          const bool ok1 = t + 1 <= r && (!has_seq || m->seq[t + 1] == seqv);
-          const float s0 = ok0 ? v[i] * __expf(dA - m->dA[t]) * m->dt[t] : 0.f;
-          const float s1 = ok1 ? v[i + 1] * __expf(dA - m->dA[t + 1]) * m->dt[t + 1] : 0.f;
-          set_word(o, i >> 1, pack_bf16(s0, s1));
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = make_uint4(0, 0, 0, 0);
+    for (int kk = 0; kk < 2; ++kk) {
+      const int k32 = half + 2 * kk;
+      uint8_t* Srow = S_sm + (k32 >> 1) * (QI * 128);
+      const int j0 = (k32 & 1) * 4;
+      if (k32 > q) {
+#pragma unroll 1
+        for (int sub = 0; sub < 4; ++sub)
+          *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) = make_uint4(0, 0, 0, 0);
+        continue;
       }
-      const int kb = k32 >> 1;
+      const int tl = k32 * 32 + lane;
+      const float dAl = m->dA[buf][tl];
+      const float dtl = m->dt[buf][tl];
+      const int sl = kk == 0 ? sl0 : sl1;
+      const bool fac = factor && k32 < q;
+      const bool diag = k32 == q;
+      const float vl = fac ? __expf(dA_R - dAl) * dtl : 0.f;
+#pragma unroll 1
+      for (int sub = 0; sub < 4; ++sub) {
+        float v[8];
+        ptx::tmem_ld8(tmem + COL_CB + k32 * 32 + sub * 8, v);
+        ptx::tmem_ld_wait();
+        if (fac) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        *reinterpret_cast<uint4*>(S_sm + kb * (QI * 128) + ptx::sw128_off(r, (k32 & 1) * 4 + j)) = o[j];
+          for (int i = 0; i < 8; ++i) {
+            const int src = sub * 8 + i;
+            float w = u * __shfl_sync(0xffffffffu, vl, src);
+            if (has_seq && __shfl_sync(0xffffffffu, sl, src) != seqv) w = 0.f;
+            v[i] *= w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int src = sub * 8 + i;
+            const float dAt = __shfl_sync(0xffffffffu, dAl, src);
+            const float dtt = __shfl_sync(0xffffffffu, dtl, src);
+            bool ok = !diag || src <= lane;
+            if (has_seq) ok = ok && (__shfl_sync(0xffffffffu, sl, src) == seqv);
+            v[i] = v[i] * __expf(ok ? dA - dAt : -INFINITY) * dtt;
+          }
+        }
+        *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) = pack8(v);
+      }
     }
     ptx::tc_fence_before();
     ptx::fence_proxy_async_smem();
@@ -361,180 +401,184 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
 }
 
 // ---------------------------------------------------------------------------
-// output worker (warps 4-7): state update in TMEM and the output epilogue
+// state worker T (warps 8-11): the inter-chunk recurrence.  Thread r owns state row
+// n = r (TMEM lane r, 64 f32 columns).  MMA_L(c) accumulates L_c onto the pre-scaled
+// state keep_c exp(dA_last_c) S_c, so after B_L(c) the columns hold S_{c+1}.
+// ---------------------------------------------------------------------------
+__device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
+  const int r = threadIdx.x & 127;
+  const int q = r >> 5, lane = r & 31;
+  const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16) + COL_ST;
+  const float Ah = a.A[h];
+  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
+  uint8_t* st_sm = sm + OFF_ST;
+  const int64_t bh = (int64_t)bi * a.H + h;
+  int prev_end = 0;
+  // decay applied to S_c before L_c is added (0 at a sequence reset, ssd rule A9)
+  auto chunk_decay = [&](int cc, const ChunkDt& cur) -> float {
+    const int64_t t0 = (int64_t)cc * QI;
+    const bool valid = t0 + r < a.L;
+    const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
+    float total;
+    int end_seq;
+    chunk_totals(dtv * Ah, cur.seq, r, last_valid, m->red_t[cc & 1], &m->end_t[cc & 1], 4, total, end_seq);
+    const bool keep = end_seq == prev_end;
+    prev_end = end_seq;
+    return keep ? __expf(total) : 0.f;
+  };
+  ChunkDt nxt = load_dt(a, bi, h, 0, r);
+  float decay = chunk_decay(0, nxt);
+  nxt = load_dt(a, bi, h, 1, r);
+  // S_0 = initial state (or 0): bf16 operand for MMA3(0), pre-scaled f32 for MMA_L(0)
+#pragma unroll 1
+  for (int j = 0; j < 8; ++j) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = a.init ? a.init[(bh * PT + 8 * j + i) * NT_ + r] : 0.f;
+    *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = pack8(v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= decay;
+    ptx::tmem_st8(tmem + 8 * j, v);
+  }
+  ptx::tmem_st_wait();
+  ptx::tc_fence_before();
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
+
+#pragma unroll 1
+  for (int c = 0; c < a.nci; ++c) {
+    const bool more = c + 1 < a.nci;
+    if (more) {
+      decay = chunk_decay(c + 1, nxt);
+      nxt = load_dt(a, bi, h, c + 2, r);
+    }
+    if (!wait_bar(m, B_L, c & 1, a.status)) return;
+    ptx::tc_fence_after();
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      float v[8];
+      ptx::tmem_ld8(tmem + 8 * j, v);
+      ptx::tmem_ld_wait();
+      if (more) {
+        *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = pack8(v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] *= decay;
+        ptx::tmem_st8(tmem + 8 * j, v);
+      } else if (a.final_states) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a.final_states[(bh * PT + 8 * j + i) * NT_ + r] = v[i];
+      }
+    }
+    if (more) {
+      ptx::tmem_st_wait();
+      ptx::tc_fence_before();
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// output worker O (warps 12-15): out[m][p] = Y + sdec_m Yi + D x, z gate; one chunk
+// behind the MMAs thanks to the double-buffered Y/Yi accumulators.
 // ---------------------------------------------------------------------------
 __device__ void out_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
-  const int r = threadIdx.x - 128;  // 0..127
+  const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
   const int64_t L = a.L, H = a.H;
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
   const float D1 = a.D_ndim == 1 ? a.D[h] : 0.f;
-  uint8_t* st_sm = sm + OFF_ST;
-  const int64_t bh = (int64_t)bi * H + h;
-
-  // state row n = r as bf16 into the MMA3 operand buffer ([n][p], 128B swizzled rows)
-  auto publish_state = [&](const float (&lo)[32], const float (&hi)[32]) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float* v = j < 4 ? lo + 8 * j : hi + 8 * (j - 4);
-      uint4 w;
-      w.x = pack_bf16(v[0], v[1]);
-      w.y = pack_bf16(v[2], v[3]);
-      w.z = pack_bf16(v[4], v[5]);
-      w.w = pack_bf16(v[6], v[7]);
-      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = w;
-    }
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[ST_FULL]);
-  };
-  {
-    float lo[32], hi[32];
-#pragma unroll
-    for (int p = 0; p < 32; ++p) {
-      lo[p] = a.init ? a.init[(bh * PT + p) * NT_ + r] : 0.f;
-      hi[p] = a.init ? a.init[(bh * PT + 32 + p) * NT_ + r] : 0.f;
-    }
-    ptx::tmem_st32(tmem + COL_ST, lo);
-    ptx::tmem_st32(tmem + COL_ST + 32, hi);
-    ptx::tmem_st_wait();
-    publish_state(lo, hi);
-  }
-
   int prev_end = 0;
   ChunkDt nxt = load_dt(a, bi, h, 0, r);
+#pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
-    const int s = c & 1;
+    const int s = c & 1, yb = c & 1;
     const int64_t t0 = (int64_t)c * QI;
     const int64_t pos = t0 + r;
     const bool valid = pos < L;
     const int64_t o0 = (((int64_t)bi * L + (valid ? pos : 0)) * H + h) * PT;
-    // z row of this chunk: issued now, used at the end of the chunk
-    uint4 zr[8];
-    if (a.z && valid) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) zr[j] = __ldg(reinterpret_cast<const uint4*>(a.z + o0) + j);
-    }
     const ChunkDt cur = nxt;
     nxt = load_dt(a, bi, h, c + 1, r);
     const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
     float cs = warp_incl_scan(dtv * Ah);
-    if (lane == 31) m->red_o[q] = cs;
+    if (lane == 31) m->red_o[c & 1][q] = cs;
     const int last_valid = (int)min((int64_t)QI - 1, L - 1 - t0);
-    if (r == last_valid) m->end_seq_o = cur.seq;
+    if (r == last_valid) m->end_o[c & 1] = cur.seq;
     ptx::named_bar_sync(2, 128);
-    for (int w = 0; w < q; ++w) cs += m->red_o[w];
-    const float dA = cs;
-    const float dA_last = m->red_o[0] + m->red_o[1] + m->red_o[2] + m->red_o[3];
-    const int end_seq = m->end_seq_o;
-    ptx::named_bar_sync(2, 128);
-    const bool keep = end_seq == prev_end;
-    const float sdec = (cur.seq == prev_end) ? __expf(dA) : 0.f;   // prev chunk's end seq
+    for (int w = 0; w < q; ++w) cs += m->red_o[c & 1][w];
+    const int end_seq = m->end_o[c & 1];
+    const float sdec = (cur.seq == prev_end) ? __expf(cs) : 0.f;   // rows continuing the previous chunk's sequence
     prev_end = end_seq;
-    const float decay = keep ? __expf(dA_last) : 0.f;
 
-    // x row for the D term (copied out so the stage can be recycled)
-    if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
-    uint4 xr[8];
+    if (!wait_bar(m, B_Y0 + yb, (c >> 1) & 1, a.status)) return;
+    ptx::tc_fence_after();
     const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) xr[j] = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
-
-    // ---- E3: S_{c+1} = decay * S_c + Lt  (TMEM), bf16 copy for the next MMA3 ----------
-    if (!wait_bar(m, B_L, c & 1, a.status)) return;
-    ptx::tc_fence_after();
-    float lo[32], hi[32], v[32];
-    ptx::tmem_ld32(tmem + COL_L, v);
-    ptx::tmem_ld32(tmem + COL_ST, lo);
-    ptx::tmem_ld_wait();
-#pragma unroll
-    for (int p = 0; p < 32; ++p) lo[p] = decay * lo[p] + v[p];
-    ptx::tmem_ld32(tmem + COL_L + 32, v);
-    ptx::tmem_ld32(tmem + COL_ST + 32, hi);
-    ptx::tmem_ld_wait();
-#pragma unroll
-    for (int p = 0; p < 32; ++p) hi[p] = decay * hi[p] + v[p];
-    ptx::tmem_st32(tmem + COL_ST, lo);
-    ptx::tmem_st32(tmem + COL_ST + 32, hi);
-    ptx::tmem_st_wait();
-    ptx::tc_fence_before();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[L_FREE]);
-    if (!wait_bar(m, B_YI, c & 1, a.status)) return;   // MMA3(c) done reading S_c
-    if (c + 1 < a.nci) publish_state(lo, hi);
-    if (c + 1 == a.nci && a.final_states) {
-#pragma unroll
-      for (int p = 0; p < 32; ++p) {
-        a.final_states[(bh * PT + p) * NT_ + r] = lo[p];
-        a.final_states[(bh * PT + 32 + p) * NT_ + r] = hi[p];
-      }
-    }
-
-    // ---- E4: out = Y + sdec * Yi + D x; z gate ------------------------------------------
-    if (!wait_bar(m, B_Y, c & 1, a.status)) return;
-    ptx::tc_fence_after();
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float y[32];
-      ptx::tmem_ld32(tmem + COL_Y + 32 * half, y);
-      ptx::tmem_ld32(tmem + COL_YI + 32 * half, v);
+    const bool zon = a.z != nullptr && valid;
+    const uint4* zp = reinterpret_cast<const uint4*>(a.z + o0);
+    uint4 zn = make_uint4(0, 0, 0, 0);
+    if (zon) zn = __ldg(zp);
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      float y[8], yi[8];
+      ptx::tmem_ld8(tmem + COL_Y0 + 128 * yb + 8 * j, y);
+      ptx::tmem_ld8(tmem + COL_YI0 + 128 * yb + 8 * j, yi);
+      const uint4 zc = zn;
+      if (zon && j < 7) zn = __ldg(zp + j + 1);
+      const uint4 xw = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
       ptx::tmem_ld_wait();
 #pragma unroll
-      for (int p = 0; p < 32; ++p) y[p] += sdec * v[p];
-      if (half == 1) {
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&m->bar[Y_FREE]);
-      }
-      if (!valid) continue;
+      for (int i = 0; i < 8; ++i) y[i] += sdec * yi[i];
       if (a.D_ndim) {
+        const uint32_t wv[4] = {xw.x, xw.y, xw.z, xw.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 w4 = xr[4 * half + j];
-          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16(wv[k]);
+          const int p = 8 * j + 2 * k;
+          y[2 * k] += (a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + p]) * f.x;
+          y[2 * k + 1] += (a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + p + 1]) * f.y;
+        }
+      }
+      if (valid) {
+        if (a.z) {
+          if (a.out_x) {
+            *reinterpret_cast<float4*>(a.out_x + o0 + 8 * j) = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4*>(a.out_x + o0 + 8 * j + 4) = make_float4(y[4], y[5], y[6], y[7]);
+          }
+          const uint32_t wv[4] = {zc.x, zc.y, zc.z, zc.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float2 f = unpack_bf16(wv[k]);
-            const int p = 8 * j + 2 * k;
-            const float d0 = a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + 32 * half + p];
-            const float d1 = a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + 32 * half + p + 1];
-            y[p] += d0 * f.x;
-            y[p + 1] += d1 * f.y;
+            y[2 * k] *= silu(f.x);
+            y[2 * k + 1] *= silu(f.y);
           }
         }
+        __stcs(reinterpret_cast<float4*>(a.out + o0 + 8 * j), make_float4(y[0], y[1], y[2], y[3]));
+        __stcs(reinterpret_cast<float4*>(a.out + o0 + 8 * j + 4), make_float4(y[4], y[5], y[6], y[7]));
       }
-      if (a.z) {
-        if (a.out_x) {
-#pragma unroll
-          for (int p = 0; p < 32; p += 4)
-            *reinterpret_cast<float4*>(a.out_x + o0 + 32 * half + p) = make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 w4 = zr[4 * half + j];
-          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16(wv[k]);
-            y[8 * j + 2 * k] *= silu(f.x);
-            y[8 * j + 2 * k + 1] *= silu(f.y);
-          }
-        }
-      }
-#pragma unroll
-      for (int p = 0; p < 32; p += 4)
-        __stcs(reinterpret_cast<float4*>(a.out + o0 + 32 * half + p), make_float4(y[p], y[p + 1], y[p + 2], y[p + 3]));
+    }
+    ptx::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
+      ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
     }
   }
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
+  uint8_t* sm = reinterpret_cast<uint8_t*>((raw + 1023) & ~uintptr_t(1023));
+  if (sm - smem_raw > (ptrdiff_t)(SMEM_LAUNCH_BYTES - SMEM_BYTES)) {
+    // the dynamic shared window is not aligned enough for the swizzled tiles: report, do nothing
+    if (threadIdx.x == 0) atomicCAS(a.status, 0u, 0x200u);
+    return;
+  }
   Misc* m = reinterpret_cast<Misc*>(sm + OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -544,28 +588,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   if (threadIdx.x == 0) {
     ptx::mbar_init(&m->bar[FULL0], 1);
     ptx::mbar_init(&m->bar[FULL1], 1);
-    ptx::mbar_init(&m->bar[EMPTY0], 9);   // MMA commit + 4 score warps + 4 output warps
-    ptx::mbar_init(&m->bar[EMPTY1], 9);
+    ptx::mbar_init(&m->bar[EMPTY0], EMPTY_COUNT);
+    ptx::mbar_init(&m->bar[EMPTY1], EMPTY_COUNT);
     ptx::mbar_init(&m->bar[B_CB], 1);
-    ptx::mbar_init(&m->bar[CB_FREE], 4);
-    ptx::mbar_init(&m->bar[B_YI], 1);
-    ptx::mbar_init(&m->bar[ST_FULL], 4);
-    ptx::mbar_init(&m->bar[XS_FULL], 4);
+    ptx::mbar_init(&m->bar[CB_FREE], 8);
+    ptx::mbar_init(&m->bar[XS_FULL], 8);
+    ptx::mbar_init(&m->bar[S_FULL], 8);
+    ptx::mbar_init(&m->bar[ST_READY], 4);
     ptx::mbar_init(&m->bar[B_L], 1);
-    ptx::mbar_init(&m->bar[L_FREE], 4);
-    ptx::mbar_init(&m->bar[S_FULL], 4);
-    ptx::mbar_init(&m->bar[B_Y], 1);
-    ptx::mbar_init(&m->bar[Y_FREE], 4);
+    ptx::mbar_init(&m->bar[B_Y0], 1);
+    ptx::mbar_init(&m->bar[B_Y1], 1);
+    ptx::mbar_init(&m->bar[Y_FREE0], 4);
+    ptx::mbar_init(&m->bar[Y_FREE1], 4);
     ptx::mbar_init(&m->bar[DRAIN], 1);
     m->abort = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == 16 && lane == 0) {
     ptx::prefetch_tmap(&a.tm_x);
     ptx::prefetch_tmap(&a.tm_b);
     ptx::prefetch_tmap(&a.tm_c);
   }
-  if (warp == 9) {
+  if (warp == 17) {
     ptx::tmem_alloc(&m->tmem_base, TMEM_COLS);
     ptx::tmem_relinquish();
   }
@@ -573,18 +617,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   __syncthreads();
   ptx::tc_fence_after();
 
-  if (warp < 4) {
-    score_worker(a, sm, m, bi, h);
-  } else if (warp < 8) {
+  if (warp < 8) {
+    score_worker(a, sm, m, bi, h, warp >> 2);
+  } else if (warp < 12) {
+    state_worker(a, sm, m, bi, h);
+  } else if (warp < 16) {
     out_worker(a, sm, m, bi, h);
-  } else if (warp == 8) {
+  } else if (warp == 16) {
     if (lane == 0) producer(a, sm, m, bi, h, g);
   } else {
     if (lane == 0) mma_issuer(a, sm, m);
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 17) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(m->tmem_base, TMEM_COLS);
   }
@@ -656,13 +702,13 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.status = (unsigned*)workspace;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(ssd_fused_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+    if (cudaFuncSetAttribute(ssd_fused_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) !=
         cudaSuccess)
       return SSD_ERR_CUDA;
     attr = true;
   }
   if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) return SSD_ERR_CUDA;
-  ssd_fused_tc_kernel<<<(unsigned)(b * H), NTHREADS, SMEM_BYTES, st>>>(a);
+  ssd_fused_tc_kernel<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? SSD_OK : SSD_ERR_CUDA;
 }
 
