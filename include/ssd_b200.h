@@ -105,6 +105,20 @@ int ssd_combined_num_launches(const ssd_fwd_params_t* p);
 int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspace_bytes,
                      ssd_stream_t stream);
 
+/* Size of the static scratch ssd_combined_fwd_noalloc uses on each GPU (16 MiB). */
+#define SSD_NOALLOC_SCRATCH_BYTES (16 << 20)
+
+/* Combined SSD forward for callers that cannot allocate device memory (no workspace slot,
+ * or cudaMalloc not allowed where they run).  No counterpart in the reference: it is
+ * ssd_combined_fwd with its scratch in a library-owned static device array of
+ * SSD_NOALLOC_SCRATCH_BYTES per GPU, reserved once this code is loaded on that GPU (at the
+ * latest by the first call there) and held until process exit.
+ * Returns SSD_ERR_WORKSPACE when ssd_combined_workspace_bytes(p) exceeds that size.
+ * The first call on a device resolves the array's address (cudaGetSymbolAddress); make it
+ * before any stream capture.  All calls on a device share the array, so calls that overlap
+ * on the GPU race; calls ordered on one stream are safe.  Allocates nothing. */
+int ssd_combined_fwd_noalloc(const ssd_fwd_params_t* p, ssd_stream_t stream);
+
 /* Stage 1.  Replaces chunk_cumsum_fwd (src/mamba2_jax/kernels/chunk_cumsum_fwd.py:288-302,
  * :194-235).  dt (b,L,H) -> dA_cumsum, dt_out (b,H,nc,Q) float32.  Padded tail
  * positions (>= L) get dt_out = 0, as the kernel path does (:228-231). */

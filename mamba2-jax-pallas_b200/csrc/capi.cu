@@ -81,6 +81,10 @@ int validate_fwd(const ssd_fwd_params_t* p) {
 
 }  // namespace
 
+namespace ssd {
+void set_last_error(const char* msg) { snprintf(g_err, sizeof(g_err), "%s", msg); }
+}  // namespace ssd
+
 extern "C" {
 
 const char* ssd_last_error(void) { return g_err; }

@@ -33,4 +33,7 @@ cudaError_t launch_chunk_state_varlen(const void* B, const void* x, int dtype, c
                                       int64_t G, int64_t N, int64_t Q, float* out, cudaStream_t st);
 cudaError_t launch_ssu(const ssu_params_t* p, cudaStream_t st);
 
+// Set the thread-local message ssd_last_error() returns.
+void set_last_error(const char* msg);
+
 }  // namespace ssd

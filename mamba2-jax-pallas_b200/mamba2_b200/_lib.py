@@ -21,6 +21,7 @@ SSD_DTYPE_F32 = 0
 SSD_DTYPE_BF16 = 1
 SSD_FLAG_FORCE_SIMT = 1
 SSD_FLAG_ROUND_STATES = 2
+SSD_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 STATUS_NAMES = {0: "SSD_OK", 1: "SSD_ERR_INVALID_ARG", 2: "SSD_ERR_UNSUPPORTED",
                 3: "SSD_ERR_ALIGNMENT", 4: "SSD_ERR_WORKSPACE", 5: "SSD_ERR_CUDA",
@@ -28,7 +29,7 @@ STATUS_NAMES = {0: "SSD_OK", 1: "SSD_ERR_INVALID_ARG", 2: "SSD_ERR_UNSUPPORTED",
 
 # Every symbol include/ssd_b200.h declares (checked by the CPU test suite).
 EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
-            "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_chunk_cumsum_fwd",
+            "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_combined_fwd_noalloc", "ssd_chunk_cumsum_fwd",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
             "ssd_last_error", "ssd_abi_version"]
@@ -88,6 +89,7 @@ def load() -> ctypes.CDLL:
     lib.ssd_combined_uses_tensor_cores.argtypes = [P(SsdFwdParams)]
     lib.ssd_combined_num_launches.argtypes = [P(SsdFwdParams)]
     lib.ssd_combined_fwd.argtypes = [P(SsdFwdParams), _vp, ctypes.c_size_t, _vp]
+    lib.ssd_combined_fwd_noalloc.argtypes = [P(SsdFwdParams), _vp]
     lib.ssd_chunk_cumsum_fwd.argtypes = [_vp, _i32, _vp, _vp, _i32, _f32, _f32, _i64, _i64, _i64,
                                          _i64, _vp, _vp, _vp]
     lib.ssd_chunk_state_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
