@@ -13,28 +13,36 @@
 //   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM (2 bufs)
 //   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM (2 bufs)
 //   E1    xs[t][p]  = x[t][p] exp(dA_last - dA_t) dt_t  (chunk-end seq only)  -> smem bf16
-//   MMA_L St[n][p] += B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM state
-//   E3    S_{c+1}   = St (already keep_c exp(dA_last_c) S_c + L_c);  bf16 -> smem for MMA3,
-//                     St <- keep_{c+1} exp(dA_last_{c+1}) S_{c+1} for the next MMA_L
+//   MMA_L Lt[n][p]  = B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM
+//   E3    S_{c+1}   = keep_c exp(dA_last_c) S_c + Lt    (TMEM f32)  -> bf16 smem for MMA3
 //   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi + D x ; * silu(z)
 // Decay factors are always formed from differences of the in-chunk cumulative sums
 // (never exp(dA_m) * exp(-dA_t)), as ssd_naive.py:264-268 does.
 //
-// The only serial dependence between chunks is the state: E3(c) -> MMA3/MMA_L(c+1) ->
-// E3(c+1).  Everything else is pipelined around it by warp role:
-//   warps 0-3  (S0) dt/dA of the chunk, half of xs and of the score blocks
-//   warps 4-7  (S1) the other halves
-//   warps 8-11 (T)  state recurrence E3
-//   warps 12-15(O)  output epilogue E4 (one chunk behind, double-buffered Y/Yi)
-//   warp 16 TMA producer, warp 17 MMA issuer.
-// Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk rows of its quadrant.
+// The only serial dependence between chunks is the state: E3(c) -> MMA3(c+1) -> E3(c+1).
+// Everything else is pipelined around it by warp role (16 warps, so every SM sub-partition
+// holds 4 warps and each thread may use 128 registers):
+//   warp 0      TMA producer (lane 0)
+//   warp 1      MMA issuer (lane 0); owns the TMEM allocation (all 512 columns)
+//   warps 2-3   prep: processed dt and cumulative dA of each chunk (shared arrays)
+//   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
+//   warps 8-11  SB: output epilogue E4 of the previous chunk (staged through the free score
+//               buffer and written by a TMA bulk store), then score column blocks 1 and 3
+//   warps 12-15 T: the state recurrence E3
+// MMA_L accumulates the chunk's state contribution L_c in its own TMEM columns, so xs and
+// MMA_L do not wait for the state chain.  Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk
+// rows of its quadrant; TMEM reads are issued 32 columns at a time with one wait, since
+// each round trip is expensive.
 // Every mbarrier wait is bounded; on timeout the CTA records SSD_ERR_TIMEOUT in the status
 // word, drains its async work and exits.
 #include <cuda.h>
+#include <cstdio>
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
 #include "ptx_sm100.cuh"
+#include "ssd_kernels.h"
 #include "ssd_tc.h"
 
 namespace ssd {
@@ -43,9 +51,9 @@ namespace {
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
 constexpr int NT_ = 128;      // state dim handled by the kernel
-constexpr int NTHREADS = 576;
+constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192, COL_ST = 384;  // Y/Yi buffer b at +128*b
+constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192, COL_ST = 384, COL_L = 448;  // Y/Yi buffer b at +128*b
 
 // shared-memory map (offsets from a 1024-aligned base)
 constexpr uint32_t SZ_C = QI * NT_ * 2;          // 32 KB  (two 64-wide swizzled boxes)
@@ -61,27 +69,25 @@ constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;   // bytes used from the 
 constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
 
 enum Bar { FULL0, FULL1, EMPTY0, EMPTY1, B_CB, CB_FREE, XS_FULL, S_FULL, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0,
-           Y_FREE1, DRAIN, NBARS };
+           Y_FREE1, DA_READY0, DA_READY1, DA_FREE0, DA_FREE1, L_FREE, OUT_READ, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t EMPTY_COUNT = 1 + 8 + 4;   // MMA commit, S0+S1 warps (xs), O warps (D x)
+constexpr uint32_t EMPTY_COUNT = 1 + 4 + 4;   // MMA commit, SA warps (xs), SB warps (D x)
+constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
   uint64_t bar[NBARS];
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
   float dt[2][QI];      // processed dt
-  float red_s[4];
-  float red_t[2][4];
-  int end_t[2];
-  float red_o[2][4];
-  int end_o[2];
+  float red_p;          // prep: warp 2's chunk total for warp 3
+  float Dv[PT];         // skip coefficient per head-dim column (0 without D)
   uint32_t tmem_base;
   volatile int abort;
 };
 static_assert(sizeof(Misc) <= MISC_BYTES, "misc area");
 
 struct TcArgs {
-  CUtensorMap tm_x, tm_b, tm_c;
+  CUtensorMap tm_x, tm_b, tm_c, tm_out;
   int L, H, G, nci;
   int dt_bf16, softplus, D_ndim;
   float lo, hi;
@@ -97,21 +103,33 @@ struct TcArgs {
   float* out_x;
   float* final_states;
   unsigned* status;
+  unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
+// Debug trace: globaltimer at phase boundaries of CTA 0, slot [role][chunk][phase].
+#define TRACE(role, c, ph)                                                                       \
+  do {                                                                                           \
+    if (a.trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (c) < 64)                      \
+      a.trace[((role) * 64 + (c)) * 16 + (ph)] = ptx::globaltimer();                             \
+  } while (0)
+
 constexpr unsigned TIMEOUT_NS = 2000000000u;  // 2 s; a normal launch takes well under 1 ms
+// The same bound in SM clock cycles (about 2 s at the B200's 1.97 GHz boost clock): the
+// cycle counter is cheap to read, the global timer is not.
+constexpr long long TIMEOUT_CYCLES = 4000000000LL;
 
 // Bounded wait.  Returns false (after flagging the CTA and the status word) on timeout or
 // when another role of this CTA already gave up.
 __device__ __forceinline__ bool wait_bar(Misc* m, int id, uint32_t parity, unsigned* status) {
   if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
-  const uint64_t t0 = ptx::globaltimer();
+  const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 32; ++i) {
       if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
+    }
     if (m->abort) return false;
-    if (ptx::globaltimer() - t0 > TIMEOUT_NS) {
+    if (clock64() - t0 > TIMEOUT_CYCLES) {
       m->abort = 1;
       atomicCAS(status, 0u, (unsigned)(0x100 | id));
       return false;
@@ -129,7 +147,7 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 }
 
 // ---------------------------------------------------------------------------
-// producer (warp 16, lane 0): C, B, x tiles of each chunk into a 2-stage ring
+// producer (warp 0, lane 0): C, B, x tiles of each chunk into a 2-stage ring
 // ---------------------------------------------------------------------------
 __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int g) {
   const uint32_t bytes = SZ_STAGE;
@@ -157,7 +175,7 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
 }
 
 // ---------------------------------------------------------------------------
-// MMA issuer (warp 17, lane 0)
+// MMA issuer (warp 1, lane 0)
 // ---------------------------------------------------------------------------
 __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   const uint32_t tmem = m->tmem_base;
@@ -181,7 +199,8 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
                    ID_CB, i > 0);
     }
     ptx::mma_commit(&m->bar[B_CB]);
-    // MMA3: Yi[yb] = C . S_c^T   (B operand = bf16 state [n][p], MN-major)
+    TRACE(4, c, 0);
+    // MMA3: Yi[yb] = C . S_c^T   (B operand = bf16 state [n][p], MN-major)  -- the state chain
     if (!wait_bar(m, ST_READY, c & 1, a.status)) break;
     if (c >= 2 && !wait_bar(m, Y_FREE0 + yb, ((c - 2) >> 1) & 1, a.status)) break;
     ptx::tc_fence_after();
@@ -191,15 +210,17 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
       ptx::mma_f16(tmem + COL_YI0 + 128 * yb, ptx::sdesc_sw128(sC + offa, 16, 1024),
                    ptx::sdesc_sw128(base + OFF_ST + i * 2048, 8192, 1024), ID_YI, i > 0);
     }
-    // MMA_L: St += B^T . xs  onto the pre-scaled state (A = B tile MN-major, B = xs MN-major)
+    // MMA_L: Lt = B^T . xs   (A = B tile read MN-major, B = xs [t][p] MN-major)
     if (!wait_bar(m, XS_FULL, c & 1, a.status)) break;
+    if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) break;
     ptx::tc_fence_after();
 #pragma unroll
     for (int i = 0; i < QI / 16; ++i) {
-      ptx::mma_f16(tmem + COL_ST, ptx::sdesc_sw128(sB + i * 2048, SZ_C / 2, 1024),
-                   ptx::sdesc_sw128(base + OFF_XS + i * 2048, 8192, 1024), ID_L, 1);
+      ptx::mma_f16(tmem + COL_L, ptx::sdesc_sw128(sB + i * 2048, SZ_C / 2, 1024),
+                   ptx::sdesc_sw128(base + OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
     }
-    ptx::mma_commit(&m->bar[B_L]);   // state S_{c+1} complete; MMA3(c) done with the bf16 state
+    ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state and MMA_L(c) with xs
+    TRACE(4, c, 1);
     // MMA2: Y[yb] = S . x   (A = scores K-major, B = x [t][p] MN-major)
     if (!wait_bar(m, S_FULL, c & 1, a.status)) break;
     ptx::tc_fence_after();
@@ -211,6 +232,7 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
     }
     ptx::mma_commit(&m->bar[B_Y0 + yb]);
     ptx::mma_commit(&m->bar[EMPTY0 + s]);
+    TRACE(4, c, 2);
   }
   // drain: wait (bounded) until every issued MMA has completed
   ptx::mma_commit(&m->bar[DRAIN]);
@@ -243,19 +265,6 @@ __device__ __forceinline__ int seq_at(const TcArgs& a, int bi, int64_t pos) {
   return (pos < a.L) ? a.seq_idx[(int64_t)bi * a.L + pos] : -1;
 }
 
-// Chunk-level values every role needs: dA_last (sum of dt*A over the chunk) and the seq id
-// at the chunk's last valid position.  One reduction through `red`/`endv` + one named
-// barrier; the caller double-buffers the slots by chunk parity.
-__device__ __forceinline__ void chunk_totals(float v, int seqv, int r, int last_valid, float* red, int* endv,
-                                             int bar_id, float& total, int& end_seq) {
-  const float w = warp_sum(v);
-  if ((r & 31) == 0) red[r >> 5] = w;
-  if (r == last_valid) *endv = seqv;
-  ptx::named_bar_sync(bar_id, 128);
-  total = red[0] + red[1] + red[2] + red[3];
-  end_seq = *endv;
-}
-
 // 16-byte word of 8 bf16, scaled by `s`, repacked.
 __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
   uint4 o;
@@ -272,76 +281,200 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// score workers S0 (warps 0-3, half 0) and S1 (warps 4-7, half 1).
-// S0 computes the chunk's processed dt and cumulative dA into shared memory; both
-// halves then build xs columns [32*half, 32*half+32) and score column blocks
-// {half, half+2} of their rows, which balances the causal triangle (quadrant q has
-// q+1 non-zero 32-column blocks) to at most two blocks per warp.
-// Loops stay rolled (8-column steps) to keep the per-chunk code small.
+// prep (warps 2-3): processed dt and in-chunk cumulative dA into the shared arrays
+// (double-buffered by chunk parity).  Thread j of the 64 owns rows 2j and 2j+1.
 // ---------------------------------------------------------------------------
+__device__ void prep_worker(const TcArgs& a, Misc* m, int bi, int h) {
+  const int j = threadIdx.x - 64;          // 0..63
+  const int lane = j & 31, w = j >> 5;     // w: 0 -> rows 0..63, 1 -> rows 64..127
+  const int r0 = 2 * j, r1 = 2 * j + 1;
+  const float Ah = a.A[h];
+  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
+  ChunkDt n0 = load_dt(a, bi, h, 0, r0), n1 = load_dt(a, bi, h, 0, r1);
+#pragma unroll 1
+  for (int c = 0; c < a.nci; ++c) {
+    const int buf = c & 1;
+    const int64_t t0 = (int64_t)c * QI;
+    const ChunkDt c0 = n0, c1 = n1;
+    n0 = load_dt(a, bi, h, c + 1, r0);
+    n1 = load_dt(a, bi, h, c + 1, r1);
+    const float d0 = (t0 + r0 < a.L) ? dt_process(c0.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    const float d1 = (t0 + r1 < a.L) ? dt_process(c1.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    float cs = warp_incl_scan((d0 + d1) * Ah);
+    // the arrays of chunk c-2 (same buffer) must be released by every reader
+    if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) return;
+    if (w == 0 && lane == 31) m->red_p = cs;
+    ptx::named_bar_sync(1, 64);
+    if (w == 1) cs += m->red_p;
+    m->dA[buf][r0] = cs - d1 * Ah;
+    m->dA[buf][r1] = cs;
+    m->dt[buf][r0] = d0;
+    m->dt[buf][r1] = d1;
+    ptx::named_bar_sync(1, 64);   // also keeps red_p from being overwritten early
+    if (lane == 0) ptx::mbar_arrive(&m->bar[DA_READY0 + buf]);
+  }
+}
+
+// Output epilogue of chunk c (run by SB): out = Y + sdec Yi + D x, z gate.  Row r is
+// staged as f32 in the (free) score buffer as two 128B-swizzled [128][32] boxes and
+// written by one TMA bulk store per box, so global writes are full lines.  The inner
+// loops carry no data-dependent branches (each costs tens of cycles when unrolled).
+template <bool HAS_Z>
+__device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tmem, int bi, int h, int c, int r,
+                             float sdec) {
+  const int yb = c & 1, s = c & 1;
+  const int lane = r & 31;
+  const int64_t pos = (int64_t)c * QI + r;
+  const bool valid = pos < a.L;
+  const int64_t o0 = (((int64_t)bi * a.L + (valid ? pos : 0)) * a.H + h) * PT;
+  float* const out_x = a.out_x;
+  const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
+  if (!wait_bar(m, B_Y0 + yb, (c >> 1) & 1, a.status)) return false;   // also: MMA2(c) done with S
+  ptx::tc_fence_after();
+  const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
+  uint8_t* stage = sm + OFF_S;
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    float y[32], yi[32];
+    ptx::tmem_ld32(tmem + COL_Y0 + 128 * yb + 32 * half, y);
+    ptx::tmem_ld32(tmem + COL_YI0 + 128 * yb + 32 * half, yi);
+    uint32_t xw[16], zw[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 xq = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * half + k));
+      xw[4 * k] = xq.x; xw[4 * k + 1] = xq.y; xw[4 * k + 2] = xq.z; xw[4 * k + 3] = xq.w;
+      if (HAS_Z) {
+        const uint4 zq = valid ? __ldg(zp + 4 * half + k) : make_uint4(0, 0, 0, 0);
+        zw[4 * k] = zq.x; zw[4 * k + 1] = zq.y; zw[4 * k + 2] = zq.z; zw[4 * k + 3] = zq.w;
+      }
+    }
+    const float* Dv = m->Dv + 32 * half;
+    ptx::tmem_ld_wait();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float2 f = unpack_bf16(xw[k]);
+      y[2 * k] = fmaf(sdec, yi[2 * k], y[2 * k]) + Dv[2 * k] * f.x;
+      y[2 * k + 1] = fmaf(sdec, yi[2 * k + 1], y[2 * k + 1]) + Dv[2 * k + 1] * f.y;
+    }
+    if (HAS_Z) {
+      if (out_x != nullptr && valid) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(out_x + o0 + 32 * half + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float2 f = unpack_bf16(zw[k]);
+        y[2 * k] *= silu(f.x);
+        y[2 * k + 1] *= silu(f.y);
+      }
+    }
+    uint8_t* box = stage + half * (QI * 128);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<float4*>(box + ptx::sw128_off(r, k)) =
+          make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
+  }
+  ptx::tc_fence_before();
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
+    ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+  }
+  ptx::named_bar_sync(2, 128);                 // all 128 rows staged
+  if (r == 0) {
+    ptx::tma_store_3d(&a.tm_out, stage, h * PT, c * QI, bi);
+    ptx::tma_store_3d(&a.tm_out, stage + QI * 128, h * PT + 32, c * QI, bi);
+    ptx::bulk_commit();
+    ptx::bulk_wait_read();                     // staging buffer read: score buffer free again
+    ptx::mbar_arrive(&m->bar[OUT_READ]);
+  }
+  ptx::named_bar_sync(2, 128);
+  return true;
+}
+
+// One 32-column block of scores for row r: v[i] holds CB[r][t] (t = 32*k32 + i) on entry.
+// FAC: t is below the quadrant's diagonal block, the decay is u_r * vl_t (vl in lane i);
+// otherwise exp(dA_r - dA_t) dt_t per element, masked to t <= r on the diagonal block.
+template <bool HAS_SEQ, bool FAC, bool DIAG>
+__device__ __forceinline__ void score_block(float (&v)[32], float u, float vl, float dA, const float* dAc,
+                                            const float* dtc, int sl, int seqv, int lane) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    bool ok = !DIAG || i <= lane;
+    if (HAS_SEQ) ok = ok && (__shfl_sync(0xffffffffu, sl, i) == seqv);
+    if (FAC) {
+      const float w = u * __shfl_sync(0xffffffffu, vl, i);
+      v[i] = ok ? v[i] * w : 0.f;
+    } else {
+      v[i] = v[i] * __expf(ok ? dA - dAc[i] : -INFINITY) * dtc[i];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// score workers SA (warps 4-7, half 0) and SB (warps 8-11, half 1).  Both build score
+// column blocks {half, half+2} of the rows of their quadrant (quadrant q has q+1 non-zero
+// blocks, so no warp does more than two).  SA also builds xs; SB first writes the output
+// of the previous chunk.
+// ---------------------------------------------------------------------------
+template <bool HAS_SEQ, bool HAS_Z>
 __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int half) {
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
   const float Ah = a.A[h];
-  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
   // Below the diagonal block the decay factors as exp(dA_r - dA_R) * exp(dA_R - dA_t)
-  // (R = first row of the warp's block) with both exponents <= 0 when the cumulative
-  // sum is non-increasing (A <= 0, dt >= 0); otherwise every element is formed directly.
+  // (R = first row of the quadrant) with both exponents <= 0 when the cumulative sum is
+  // non-increasing (A <= 0, dt >= 0); otherwise every element is formed directly.
   const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
-  const bool has_seq = a.seq_idx != nullptr;
+  constexpr bool has_seq = HAS_SEQ;
   uint8_t* S_sm = sm + OFF_S;
   uint8_t* xs_sm = sm + OFF_XS;
-  ChunkDt nxt = half == 0 ? load_dt(a, bi, h, 0, r) : ChunkDt{0.f, 0};
+  float sdec_prev = 0.f;
 #pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
-    const int s = c & 1, buf = c & 1;
+    const int buf = c & 1, s = c & 1;
     const int64_t t0 = (int64_t)c * QI;
-    const bool valid = t0 + r < a.L;
-    if (half == 0) {
-      const ChunkDt cur = nxt;
-      nxt = load_dt(a, bi, h, c + 1, r);
-      const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-      float cs = warp_incl_scan(dtv * Ah);
-      if (lane == 31) m->red_s[q] = cs;
-      ptx::named_bar_sync(1, 128);
-      for (int w = 0; w < q; ++w) cs += m->red_s[w];
-      m->dA[buf][r] = cs;
-      m->dt[buf][r] = dtv;
-    }
-    ptx::named_bar_sync(3, 256);
-    const float dA = m->dA[buf][r];
-    const float dtv = m->dt[buf][r];
-    const float dA_last = m->dA[buf][QI - 1];
+    if (half == 1 && c > 0 && !output_chunk<HAS_Z>(a, sm, m, tmem, bi, h, c - 1, r, sdec_prev)) return;
+    int seqv = (t0 + r < a.L) ? 0 : -1, prev_seq = 0, end_seq = 0, sl0 = 0, sl1 = 0;
     const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
-    int seqv = valid ? 0 : -1, end_seq = 0, sl0 = 0, sl1 = 0;
     if (has_seq) {
       seqv = seq_at(a, bi, t0 + r);
+      prev_seq = c == 0 ? 0 : seq_at(a, bi, t0 - 1);
       end_seq = seq_at(a, bi, t0 + last_valid);
       sl0 = seq_at(a, bi, t0 + half * 32 + lane);
       sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
     }
-    const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(dA_last - dA) * dtv : 0.f;
+    if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
+    const float dA = m->dA[buf][r];
 
-    // ---- E1: xs = x * scale (this half's 4 16-byte words of row r) -----------------
-    if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
-    if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
-    const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-#pragma unroll 1
-    for (int j = 4 * half; j < 4 * half + 4; ++j) {
-      const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
-      *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, j)) = scale_row16(w, scale);
-    }
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      ptx::mbar_arrive(&m->bar[XS_FULL]);
-      ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+    if (half == 0) {
+      // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
+      const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(m->dA[buf][QI - 1] - dA) * m->dt[buf][r] : 0.f;
+      if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
+      if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
+      const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, k)) =
+            scale_row16(*reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, k)), scale);
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::mbar_arrive(&m->bar[XS_FULL]);
+        ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+      }
+      // the score buffer still holds the previous chunk's staged output until its bulk
+      // store has read it
+      if (c > 0 && !wait_bar(m, OUT_READ, (c - 1) & 1, a.status)) return;
     }
 
     // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
+    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 6);
     if (!wait_bar(m, B_CB, c & 1, a.status)) return;
-    if (c > 0 && !wait_bar(m, B_Y0 + ((c - 1) & 1), ((c - 1) >> 1) & 1, a.status)) return;  // MMA2(c-1) done with S
+    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 7);
     ptx::tc_fence_after();
     const float dA_R = m->dA[buf][q * 32];
     const float u = __expf(dA - dA_R);
@@ -351,95 +484,71 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       uint8_t* Srow = S_sm + (k32 >> 1) * (QI * 128);
       const int j0 = (k32 & 1) * 4;
       if (k32 > q) {
-#pragma unroll 1
+#pragma unroll
         for (int sub = 0; sub < 4; ++sub)
           *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) = make_uint4(0, 0, 0, 0);
         continue;
       }
       const int tl = k32 * 32 + lane;
-      const float dAl = m->dA[buf][tl];
-      const float dtl = m->dt[buf][tl];
       const int sl = kk == 0 ? sl0 : sl1;
       const bool fac = factor && k32 < q;
       const bool diag = k32 == q;
-      const float vl = fac ? __expf(dA_R - dAl) * dtl : 0.f;
-#pragma unroll 1
-      for (int sub = 0; sub < 4; ++sub) {
-        float v[8];
-        ptx::tmem_ld8(tmem + COL_CB + k32 * 32 + sub * 8, v);
-        ptx::tmem_ld_wait();
-        if (fac) {
+      const float vl = fac ? __expf(dA_R - m->dA[buf][tl]) * m->dt[buf][tl] : 0.f;
+      const float* dAc = m->dA[buf] + k32 * 32;
+      const float* dtc = m->dt[buf] + k32 * 32;
+      float v[32];
+      ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);   // one TMEM round trip per block
+      ptx::tmem_ld_wait();
+      if (fac) score_block<HAS_SEQ, true, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
+      else if (diag) score_block<HAS_SEQ, false, true>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
+      else score_block<HAS_SEQ, false, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int src = sub * 8 + i;
-            float w = u * __shfl_sync(0xffffffffu, vl, src);
-            if (has_seq && __shfl_sync(0xffffffffu, sl, src) != seqv) w = 0.f;
-            v[i] *= w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int src = sub * 8 + i;
-            const float dAt = __shfl_sync(0xffffffffu, dAl, src);
-            const float dtt = __shfl_sync(0xffffffffu, dtl, src);
-            bool ok = !diag || src <= lane;
-            if (has_seq) ok = ok && (__shfl_sync(0xffffffffu, sl, src) == seqv);
-            v[i] = v[i] * __expf(ok ? dA - dAt : -INFINITY) * dtt;
-          }
-        }
-        *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) = pack8(v);
-      }
+      for (int sub = 0; sub < 4; ++sub)
+        *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) =
+            make_uint4(pack_bf16(v[8 * sub], v[8 * sub + 1]), pack_bf16(v[8 * sub + 2], v[8 * sub + 3]),
+                       pack_bf16(v[8 * sub + 4], v[8 * sub + 5]), pack_bf16(v[8 * sub + 6], v[8 * sub + 7]));
     }
+    // rows continuing the previous chunk's sequence read the passed state (rule A9)
+    sdec_prev = (seqv == prev_seq) ? __expf(dA) : 0.f;
     ptx::tc_fence_before();
     ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
       ptx::mbar_arrive(&m->bar[CB_FREE]);
       ptx::mbar_arrive(&m->bar[S_FULL]);
+      ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     }
+    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 8);
+    if ((r == 0 || r == 96) && half == 0) TRACE(r == 0 ? 0 : 1, c, 8);
+  }
+  if (half == 1 && a.nci > 0) {
+    if (!output_chunk<HAS_Z>(a, sm, m, tmem, bi, h, a.nci - 1, r, sdec_prev)) return;
+    if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
   }
 }
 
 // ---------------------------------------------------------------------------
-// state worker T (warps 8-11): the inter-chunk recurrence.  Thread r owns state row
-// n = r (TMEM lane r, 64 f32 columns).  MMA_L(c) accumulates L_c onto the pre-scaled
-// state keep_c exp(dA_last_c) S_c, so after B_L(c) the columns hold S_{c+1}.
+// state worker T (warps 12-15): S_{c+1} = keep_c exp(dA_last_c) S_c + L_c.  Thread r owns
+// state row n = r (TMEM lane r): 64 f32 columns of the state and of L_c.
 // ---------------------------------------------------------------------------
 __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
-  const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16) + COL_ST;
-  const float Ah = a.A[h];
-  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
+  const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
   uint8_t* st_sm = sm + OFF_ST;
   const int64_t bh = (int64_t)bi * a.H + h;
-  int prev_end = 0;
-  // decay applied to S_c before L_c is added (0 at a sequence reset, ssd rule A9)
-  auto chunk_decay = [&](int cc, const ChunkDt& cur) -> float {
-    const int64_t t0 = (int64_t)cc * QI;
-    const bool valid = t0 + r < a.L;
-    const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
-    float total;
-    int end_seq;
-    chunk_totals(dtv * Ah, cur.seq, r, last_valid, m->red_t[cc & 1], &m->end_t[cc & 1], 4, total, end_seq);
-    const bool keep = end_seq == prev_end;
-    prev_end = end_seq;
-    return keep ? __expf(total) : 0.f;
-  };
-  ChunkDt nxt = load_dt(a, bi, h, 0, r);
-  float decay = chunk_decay(0, nxt);
-  nxt = load_dt(a, bi, h, 1, r);
-  // S_0 = initial state (or 0): bf16 operand for MMA3(0), pre-scaled f32 for MMA_L(0)
+  // S_0 = initial state (or 0): f32 in TMEM, bf16 operand for MMA3(0)
 #pragma unroll 1
-  for (int j = 0; j < 8; ++j) {
-    float v[8];
+  for (int half = 0; half < 2; ++half) {
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = a.init ? a.init[(bh * PT + 8 * j + i) * NT_ + r] : 0.f;
-    *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = pack8(v);
+    for (int i = 0; i < 32; ++i) v[i] = a.init ? a.init[(bh * PT + 32 * half + i) * NT_ + r] : 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] *= decay;
-    ptx::tmem_st8(tmem + 8 * j, v);
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, 4 * half + j)) =
+          make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                     pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    ptx::tmem_st32(tl + COL_ST + 32 * half, v);
   }
   ptx::tmem_st_wait();
   ptx::tc_fence_before();
@@ -447,133 +556,64 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   __syncwarp();
   if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
 
+  int prev_end = 0;
 #pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
+    const int buf = c & 1;
     const bool more = c + 1 < a.nci;
-    if (more) {
-      decay = chunk_decay(c + 1, nxt);
-      nxt = load_dt(a, bi, h, c + 2, r);
-    }
-    if (!wait_bar(m, B_L, c & 1, a.status)) return;
+    // chunk decay: 0 when the chunk-end sequence id changes (state_passing_fwd.py:208-225;
+    // the id before the first chunk counts as 0)
+    const int64_t t0 = (int64_t)c * QI;
+    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
+    const int end_seq = a.seq_idx ? seq_at(a, bi, t0 + last_valid) : 0;
+    if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
+    const float dA_last = m->dA[buf][QI - 1];
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
+    const float decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
+    prev_end = end_seq;
+    if (r == 0) TRACE(2, c, 0);
+    if (!wait_bar(m, B_L, c & 1, a.status)) return;   // L_c ready, MMA3(c) done with S_c
+    if (r == 0) TRACE(2, c, 1);
     ptx::tc_fence_after();
 #pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      float v[8];
-      ptx::tmem_ld8(tmem + 8 * j, v);
+    for (int half = 0; half < 2; ++half) {
+      float sv[32], lv[32];
+      ptx::tmem_ld32(tl + COL_ST + 32 * half, sv);
+      ptx::tmem_ld32(tl + COL_L + 32 * half, lv);
       ptx::tmem_ld_wait();
-      if (more) {
-        *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, j)) = pack8(v);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] *= decay;
-        ptx::tmem_st8(tmem + 8 * j, v);
+      for (int i = 0; i < 32; ++i) sv[i] = decay * sv[i] + lv[i];
+      if (more) {
+        ptx::tmem_st32(tl + COL_ST + 32 * half, sv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, 4 * half + j)) =
+              make_uint4(pack_bf16(sv[8 * j], sv[8 * j + 1]), pack_bf16(sv[8 * j + 2], sv[8 * j + 3]),
+                         pack_bf16(sv[8 * j + 4], sv[8 * j + 5]), pack_bf16(sv[8 * j + 6], sv[8 * j + 7]));
       } else if (a.final_states) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a.final_states[(bh * PT + 8 * j + i) * NT_ + r] = v[i];
+        for (int i = 0; i < 32; ++i) a.final_states[(bh * PT + 32 * half + i) * NT_ + r] = sv[i];
       }
     }
-    if (more) {
-      ptx::tmem_st_wait();
-      ptx::tc_fence_before();
-      ptx::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// output worker O (warps 12-15): out[m][p] = Y + sdec_m Yi + D x, z gate; one chunk
-// behind the MMAs thanks to the double-buffered Y/Yi accumulators.
-// ---------------------------------------------------------------------------
-__device__ void out_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
-  const int r = threadIdx.x & 127;
-  const int q = r >> 5, lane = r & 31;
-  const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
-  const int64_t L = a.L, H = a.H;
-  const float Ah = a.A[h];
-  const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  const float D1 = a.D_ndim == 1 ? a.D[h] : 0.f;
-  int prev_end = 0;
-  ChunkDt nxt = load_dt(a, bi, h, 0, r);
-#pragma unroll 1
-  for (int c = 0; c < a.nci; ++c) {
-    const int s = c & 1, yb = c & 1;
-    const int64_t t0 = (int64_t)c * QI;
-    const int64_t pos = t0 + r;
-    const bool valid = pos < L;
-    const int64_t o0 = (((int64_t)bi * L + (valid ? pos : 0)) * H + h) * PT;
-    const ChunkDt cur = nxt;
-    nxt = load_dt(a, bi, h, c + 1, r);
-    const float dtv = valid ? dt_process(cur.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-    float cs = warp_incl_scan(dtv * Ah);
-    if (lane == 31) m->red_o[c & 1][q] = cs;
-    const int last_valid = (int)min((int64_t)QI - 1, L - 1 - t0);
-    if (r == last_valid) m->end_o[c & 1] = cur.seq;
-    ptx::named_bar_sync(2, 128);
-    for (int w = 0; w < q; ++w) cs += m->red_o[c & 1][w];
-    const int end_seq = m->end_o[c & 1];
-    const float sdec = (cur.seq == prev_end) ? __expf(cs) : 0.f;   // rows continuing the previous chunk's sequence
-    prev_end = end_seq;
-
-    if (!wait_bar(m, B_Y0 + yb, (c >> 1) & 1, a.status)) return;
-    ptx::tc_fence_after();
-    const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-    const bool zon = a.z != nullptr && valid;
-    const uint4* zp = reinterpret_cast<const uint4*>(a.z + o0);
-    uint4 zn = make_uint4(0, 0, 0, 0);
-    if (zon) zn = __ldg(zp);
-#pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      float y[8], yi[8];
-      ptx::tmem_ld8(tmem + COL_Y0 + 128 * yb + 8 * j, y);
-      ptx::tmem_ld8(tmem + COL_YI0 + 128 * yb + 8 * j, yi);
-      const uint4 zc = zn;
-      if (zon && j < 7) zn = __ldg(zp + j + 1);
-      const uint4 xw = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, j));
-      ptx::tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] += sdec * yi[i];
-      if (a.D_ndim) {
-        const uint32_t wv[4] = {xw.x, xw.y, xw.z, xw.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = unpack_bf16(wv[k]);
-          const int p = 8 * j + 2 * k;
-          y[2 * k] += (a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + p]) * f.x;
-          y[2 * k + 1] += (a.D_ndim == 1 ? D1 : a.D[(int64_t)h * PT + p + 1]) * f.y;
-        }
-      }
-      if (valid) {
-        if (a.z) {
-          if (a.out_x) {
-            *reinterpret_cast<float4*>(a.out_x + o0 + 8 * j) = make_float4(y[0], y[1], y[2], y[3]);
-            *reinterpret_cast<float4*>(a.out_x + o0 + 8 * j + 4) = make_float4(y[4], y[5], y[6], y[7]);
-          }
-          const uint32_t wv[4] = {zc.x, zc.y, zc.z, zc.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16(wv[k]);
-            y[2 * k] *= silu(f.x);
-            y[2 * k + 1] *= silu(f.y);
-          }
-        }
-        __stcs(reinterpret_cast<float4*>(a.out + o0 + 8 * j), make_float4(y[0], y[1], y[2], y[3]));
-        __stcs(reinterpret_cast<float4*>(a.out + o0 + 8 * j + 4), make_float4(y[4], y[5], y[6], y[7]));
-      }
-    }
+    if (more) ptx::tmem_st_wait();
     ptx::tc_fence_before();
+    if (more) ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
-      ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+      ptx::mbar_arrive(&m->bar[L_FREE]);
+      if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
     }
+    if (r == 0) TRACE(2, c, 2);
   }
 }
 
+template <bool HAS_SEQ, bool HAS_Z>
 __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
-  uint8_t* sm = reinterpret_cast<uint8_t*>((raw + 1023) & ~uintptr_t(1023));
+  // Align by pointer arithmetic on the shared array itself (not through an integer cast)
+  // so that every access below stays a shared-space load/store.
+  uint8_t* sm = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
   if (sm - smem_raw > (ptrdiff_t)(SMEM_LAUNCH_BYTES - SMEM_BYTES)) {
     // the dynamic shared window is not aligned enough for the swizzled tiles: report, do nothing
     if (threadIdx.x == 0) atomicCAS(a.status, 0u, 0x200u);
@@ -592,7 +632,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[EMPTY1], EMPTY_COUNT);
     ptx::mbar_init(&m->bar[B_CB], 1);
     ptx::mbar_init(&m->bar[CB_FREE], 8);
-    ptx::mbar_init(&m->bar[XS_FULL], 8);
+    ptx::mbar_init(&m->bar[XS_FULL], 4);
     ptx::mbar_init(&m->bar[S_FULL], 8);
     ptx::mbar_init(&m->bar[ST_READY], 4);
     ptx::mbar_init(&m->bar[B_L], 1);
@@ -600,16 +640,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[B_Y1], 1);
     ptx::mbar_init(&m->bar[Y_FREE0], 4);
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
+    ptx::mbar_init(&m->bar[DA_READY0], 2);
+    ptx::mbar_init(&m->bar[DA_READY1], 2);
+    ptx::mbar_init(&m->bar[DA_FREE0], DA_FREE_COUNT);
+    ptx::mbar_init(&m->bar[DA_FREE1], DA_FREE_COUNT);
+    ptx::mbar_init(&m->bar[L_FREE], 4);
+    ptx::mbar_init(&m->bar[OUT_READ], 1);
     ptx::mbar_init(&m->bar[DRAIN], 1);
     m->abort = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 16 && lane == 0) {
+  if (threadIdx.x < PT)
+    m->Dv[threadIdx.x] = a.D_ndim == 1 ? a.D[h] : a.D_ndim == 2 ? a.D[(int64_t)h * PT + threadIdx.x] : 0.f;
+  if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&a.tm_x);
     ptx::prefetch_tmap(&a.tm_b);
     ptx::prefetch_tmap(&a.tm_c);
+    ptx::prefetch_tmap(&a.tm_out);
   }
-  if (warp == 17) {
+  if (warp == 1) {
     ptx::tmem_alloc(&m->tmem_base, TMEM_COLS);
     ptx::tmem_relinquish();
   }
@@ -617,20 +666,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   __syncthreads();
   ptx::tc_fence_after();
 
-  if (warp < 8) {
-    score_worker(a, sm, m, bi, h, warp >> 2);
-  } else if (warp < 12) {
-    state_worker(a, sm, m, bi, h);
-  } else if (warp < 16) {
-    out_worker(a, sm, m, bi, h);
-  } else if (warp == 16) {
+  if (warp == 0) {
     if (lane == 0) producer(a, sm, m, bi, h, g);
-  } else {
+  } else if (warp == 1) {
     if (lane == 0) mma_issuer(a, sm, m);
+  } else if (warp < 4) {
+    prep_worker(a, m, bi, h);
+  } else if (warp < 12) {
+    score_worker<HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
+  } else {
+    state_worker(a, sm, m, bi, h);
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 17) {
+  if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(m->tmem_base, TMEM_COLS);
   }
@@ -655,15 +704,18 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 map over (inner = cols, rows = L, batch) with a 64 x 128 x 1 box, 128B swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint64_t b) {
+// 3-D map over (inner = cols, rows = L, batch) with a (128 bytes) x 128 x 1 box, 128B swizzle:
+// bf16 boxes are 64 columns wide, f32 boxes 32.
+bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint64_t b, bool f32 = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
+  const uint64_t es_bytes = f32 ? 4 : 2;
   cuuint64_t dims[3] = {cols, L, b};
-  cuuint64_t strides[2] = {cols * 2, cols * L * 2};
-  cuuint32_t box[3] = {64, (cuuint32_t)QI, 1};
+  cuuint64_t strides[2] = {cols * es_bytes, cols * L * es_bytes};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es_bytes), (cuuint32_t)QI, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+  return fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+            dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -682,7 +734,19 @@ bool tc_supported(const ssd_fwd_params_t* p) {
   return encode_fn() != nullptr;
 }
 
-size_t tc_workspace_bytes(const ssd_fwd_params_t* p) { return tc_supported(p) ? 256 : 0; }
+bool trace_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("SSD_TC_TRACE");
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on == 1;
+}
+
+// 256 bytes: device status word; with SSD_TC_TRACE=1 a 64 KB phase trace follows (debug).
+size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
+  return tc_supported(p) ? 256 + (trace_enabled() ? 8 * 64 * 16 * 8 : 0) : 0;
+}
 
 int tc_num_launches(const ssd_fwd_params_t*) { return 1; }
 
@@ -691,8 +755,11 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   memset(&a, 0, sizeof(a));
   const int64_t b = p->batch, L = p->seqlen, H = p->nheads, G = p->ngroups;
   if (!make_map(&a.tm_x, p->x, (uint64_t)H * PT, L, b) || !make_map(&a.tm_b, p->B, (uint64_t)G * NT_, L, b) ||
-      !make_map(&a.tm_c, p->C, (uint64_t)G * NT_, L, b))
+      !make_map(&a.tm_c, p->C, (uint64_t)G * NT_, L, b) ||
+      !make_map(&a.tm_out, p->out, (uint64_t)H * PT, L, b, true)) {
+    set_last_error("cuTensorMapEncodeTiled failed for x/B/C/out");
     return SSD_ERR_CUDA;
+  }
   a.L = (int)L; a.H = (int)H; a.G = (int)G; a.nci = (int)((L + QI - 1) / QI);
   a.dt_bf16 = p->dt_dtype == SSD_DTYPE_BF16; a.softplus = p->dt_softplus; a.D_ndim = p->D ? p->D_ndim : 0;
   a.lo = p->dt_min; a.hi = p->dt_max;
@@ -700,16 +767,33 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.x = (const bf16*)p->x; a.z = (const bf16*)p->z; a.init = p->initial_states; a.seq_idx = p->seq_idx;
   a.out = p->out; a.out_x = p->z ? p->out_x : nullptr; a.final_states = p->final_states;
   a.status = (unsigned*)workspace;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(ssd_fused_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) !=
-        cudaSuccess)
+  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256) : nullptr;
+  typedef void (*KernelFn)(TcArgs);
+  static const KernelFn kernels[4] = {ssd_fused_tc_kernel<false, false>, ssd_fused_tc_kernel<false, true>,
+                                      ssd_fused_tc_kernel<true, false>, ssd_fused_tc_kernel<true, true>};
+  static bool attr[4] = {false, false, false, false};
+  const int kid = (p->seq_idx ? 2 : 0) + (p->z ? 1 : 0);
+  const KernelFn kern = kernels[kid];
+  if (!attr[kid]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) != cudaSuccess) {
+      set_last_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
       return SSD_ERR_CUDA;
-    attr = true;
+    }
+    attr[kid] = true;
   }
-  if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) return SSD_ERR_CUDA;
-  ssd_fused_tc_kernel<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SSD_OK : SSD_ERR_CUDA;
+  if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) {
+    set_last_error("cudaMemsetAsync of the status word failed");
+    return SSD_ERR_CUDA;
+  }
+  kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "ssd_fused_tc_kernel launch: %s", cudaGetErrorString(e));
+    set_last_error(msg);
+    return SSD_ERR_CUDA;
+  }
+  return SSD_OK;
 }
 
 }  // namespace ssd
