@@ -126,10 +126,95 @@ __global__ void __launch_bounds__(SSU_THREADS) ssu_kernel(const SsuArgs a) {
   }
 }
 
+
+// Fast path for the common decode shapes (N % 128 == 0, P % 8 == 0, A / dt / D / dt_bias
+// per head).  Each warp owns 8 state rows and issues every load it needs before any math:
+// 8 x 16 B of state per lane (per 128 state columns), its slice of B and C, the 8 x values
+// as one vector load and the head's dt.  No shared memory, no block barrier, ~64 registers,
+// so several CTAs per SM keep enough bytes in flight to stream the state at HBM rate.
+template <typename T, typename TDT, int NV>
+__global__ void __launch_bounds__(SSU_THREADS) ssu_fast_kernel(const SsuArgs a) {
+  const int64_t bh = blockIdx.x;
+  const int64_t bi = bh / a.H, h = bh % a.H;
+  const int64_t g = h / (a.H / a.G);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int NW = SSU_THREADS / 32;
+  const float Ah = a.A[h];
+  const float bias = a.bias_ndim ? a.dt_bias[h] : 0.f;
+  const float Dh = a.D_ndim ? a.D[h] : 0.f;
+  float d = ldg((const TDT*)a.dt + bh) + bias;
+  if (a.softplus) d = softplus_jax(d);
+  const float dA = expf(d * Ah);
+  float Bv[NV][4], Cv[NV][4];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int64_t n0 = (int64_t)(v * 32 + lane) * 4;
+    const T* Bp = (const T*)a.B + (bi * a.G + g) * a.N + n0;
+    const T* Cp = (const T*)a.C + (bi * a.G + g) * a.N + n0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      Bv[v][i] = ldg(Bp + i);
+      Cv[v][i] = ldg(Cp + i);
+    }
+  }
+  for (int64_t p0 = (int64_t)warp * 8; p0 < a.P; p0 += (int64_t)NW * 8) {
+    float* S = a.state + (bh * a.P + p0) * a.N;
+    float4 s[8][NV];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) s[r][v] = __ldcs(reinterpret_cast<const float4*>(S + r * a.N) + v * 32 + lane);
+    float xv[8], zv[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      xv[r] = ldg((const T*)a.x + bh * a.P + p0 + r);
+      zv[r] = a.z ? ldg((const T*)a.z + bh * a.P + p0 + r) : 0.f;
+    }
+    float acc[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float dx = d * xv[r];
+      float t = 0.f;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        float4 o;
+        o.x = fmaf(s[r][v].x, dA, dx * Bv[v][0]);
+        o.y = fmaf(s[r][v].y, dA, dx * Bv[v][1]);
+        o.z = fmaf(s[r][v].z, dA, dx * Bv[v][2]);
+        o.w = fmaf(s[r][v].w, dA, dx * Bv[v][3]);
+        __stcs(reinterpret_cast<float4*>(S + r * a.N) + v * 32 + lane, o);
+        t += o.x * Cv[v][0] + o.y * Cv[v][1] + o.z * Cv[v][2] + o.w * Cv[v][3];
+      }
+      acc[r] = t;
+    }
+    // reduce the 8 row sums across the warp; lane r ends with row r's total
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[r] = warp_sum(acc[r]);
+    if (lane < 8) {
+      float o = acc[0], xo = xv[0], zo = zv[0];
+#pragma unroll
+      for (int r = 1; r < 8; ++r)
+        if (lane == r) {
+          o = acc[r];
+          xo = xv[r];
+          zo = zv[r];
+        }
+      o += Dh * xo;
+      if (a.z) o *= silu(zo);
+      a.out[bh * a.P + p0 + lane] = o;
+    }
+  }
+}
+
 template <typename T, typename TDT>
 void ssu_launch_t(const SsuArgs& a, int64_t grid, bool vec, cudaStream_t st) {
   const size_t smem = 2 * a.N * sizeof(float);
-  if (vec)
+  const bool fast = vec && a.A_ndim == 1 && a.dt_ndim == 2 && a.D_ndim <= 1 && a.bias_ndim <= 1 &&
+                    a.P % 8 == 0 && (a.N == 128 || a.N == 256);
+  if (fast) {
+    if (a.N == 128) ssu_fast_kernel<T, TDT, 1><<<(unsigned)grid, SSU_THREADS, 0, st>>>(a);
+    else ssu_fast_kernel<T, TDT, 2><<<(unsigned)grid, SSU_THREADS, 0, st>>>(a);
+  } else if (vec)
     ssu_kernel<T, TDT, true><<<(unsigned)grid, SSU_THREADS, smem, st>>>(a);
   else
     ssu_kernel<T, TDT, false><<<(unsigned)grid, SSU_THREADS, smem, st>>>(a);

@@ -260,6 +260,8 @@ SSU_CASES = [
     (3, 6, 32, 3, 64, "f32", 3, 3, 2, 2, True, True),      # per-element dt/A/D/bias
     (2, 4, 16, 2, 18, "bf16", 2, 1, 1, 1, False, True),    # N % 4 != 0 (scalar path)
     (1, 8, 70, 4, 256, "bf16", 3, 1, 0, 0, True, False),   # P not a multiple of 8
+    (3, 8, 64, 2, 256, "bf16", 2, 1, 1, 1, True, True),    # N=256 fast path
+    (2, 4, 32, 4, 128, "f32", 2, 1, 0, 0, False, True),    # fast path, no D / z / bias
 ]
 
 
