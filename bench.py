@@ -17,9 +17,7 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
-import tempfile
 import time
 
 _REPO = os.path.dirname(os.path.abspath(__file__))
@@ -43,6 +41,15 @@ def _peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def measured_traffic(key):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(_REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)[key]["traffic_bytes"]
+    except Exception:
+        return None
+
+
 def layer_work(cfg):
     """Algorithmic FLOPs and HBM bytes of one SSD layer forward (causal FLOPs; fp32 out)."""
     b, L, H, P, G, N, Q = (cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.ngroups,
@@ -63,45 +70,55 @@ def layer_work(cfg):
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled through NVML every ~2 ms on a background thread
+    while the timed region runs (nvidia-smi's 100 ms floor misses short regions)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, index):
-        self.index = index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-i", str(index), "-lms", "200"], stdout=self.f,
-                                      stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = torch.cuda.get_device_properties(index).uuid
+            h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(hi)
+                u = u.decode() if isinstance(u, bytes) else u
+                if str(uuid) in u:
+                    h = hi
+            h = h or pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._nv, self._h = pynvml, h
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
         except Exception:
-            self.p = None
+            self._nv = None
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.reasons.update(n for bit, n in self.REASONS.items() if mask & bit)
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def stop(self):
-        if self.p is None:
+        if self._nv is None:
             return None
-        self.p.terminate()
-        try:
-            self.p.wait(5)
-        except Exception:
-            self.p.kill()
-        self.f.flush()
-        rows = []
-        with open(self.f.name) as fh:
-            for line in fh:
-                c = [x.strip() for x in line.split(",")]
-                if len(c) >= 9:
-                    rows.append(c)
-        os.unlink(self.f.name)
-        if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+        self._stop.set()
+        self._t.join(1.0)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def dev_inputs(inp, cfg, device):
@@ -318,8 +335,9 @@ def run_ours(args, cfg, rank, world, device):
                        "parallelism": f"batch-sharded x{world}, no collective",
                        "l2": f"{N_SETS} rotated input sets, each step's inputs+outputs > L2"},
             "roofline": {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
-                         "frac": ach / peak, "peak_kind": peak_kind, "traffic": None,
-                         "kernel_ms": kms},
+                         "frac": ach / peak, "peak_kind": peak_kind,
+                         "traffic": measured_traffic(f"{name}/{args.config}") if not args.override else None,
+                         "algorithmic_bytes": kbytes, "kernel_ms": kms},
             "layer_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": 1e3 * ms / args.steps,
                                "frac": t_roof / (ms / args.steps / 1e3), "flops": flops, "bytes": byts},
             "kernels": {r[0]: round(r[1] * 1e3, 2) for r in brk},
@@ -404,7 +422,9 @@ def run_ssu(args, rank, world, device):
                        "ngroups": G, "dstate": N, "input_dtype": "bf16", "state": "f32 in place",
                        "l2": f"state {state_bytes / 1e9:.2f} GB > L2"},
             "roofline": {"kernel": "ssu_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                         "frac": ach / hbm, "peak_kind": peak_kind, "traffic": None},
+                         "frac": ach / hbm, "peak_kind": peak_kind,
+                         "traffic": measured_traffic("ssu_kernel/c4") if not args.override else None,
+                         "algorithmic_bytes": step_bytes},
             "e2e": {"value": e2e_steps * b * world / (ms_e2e / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4},
             "gpu_launches": steps, "clocks": clocks}
@@ -419,8 +439,15 @@ def main():
     ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--override", action="append", default=[],
+                    help="key=value on the config (e.g. batch=32) for small profiling cases")
     args = ap.parse_args()
     cfg = S.CONFIGS[args.config]
+    if args.override:
+        import dataclasses
+        kv = dict(o.split("=", 1) for o in args.override)
+        cfg = dataclasses.replace(cfg, **{k: type(getattr(cfg, k))(v) for k, v in kv.items()})
+        S.CONFIGS[args.config] = cfg
     if args.impl == "reference" and args.config == "c4":
         raise SystemExit("reference arm for c4 not implemented")
     world = int(os.environ.get("WORLD_SIZE", "1"))
