@@ -24,7 +24,7 @@
 // holds 4 warps and each thread may use 128 registers):
 //   warp 0      TMA producer (lane 0)
 //   warp 1      MMA issuer (lane 0); owns the TMEM allocation (all 512 columns)
-//   warps 2-3   prep: processed dt and cumulative dA of each chunk (shared arrays)
+//   warp 2      prep: processed dt and cumulative dA of each chunk (shared arrays); warp 3 spare
 //   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
 //   warps 8-11  SB: output epilogue E4 of the previous chunk (staged through the free score
 //               buffer and written by a TMA bulk store), then score column blocks 1 and 3
@@ -50,36 +50,49 @@ namespace {
 
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
-constexpr int NT_ = 128;      // state dim handled by the kernel
 constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192, COL_ST = 384, COL_L = 448;  // Y/Yi buffer b at +128*b
-
-// shared-memory map (offsets from a 1024-aligned base)
-constexpr uint32_t SZ_C = QI * NT_ * 2;          // 32 KB  (two 64-wide swizzled boxes)
-constexpr uint32_t SZ_X = QI * PT * 2;           // 16 KB
-constexpr uint32_t SZ_STAGE = 2 * SZ_C + SZ_X;   // C, B, x
-constexpr uint32_t OFF_STAGE = 0;
-constexpr uint32_t OFF_S = 2 * SZ_STAGE;         // scores, 32 KB (two K-blocks)
-constexpr uint32_t OFF_XS = OFF_S + QI * QI * 2; // 16 KB
-constexpr uint32_t OFF_ST = OFF_XS + SZ_X;       // state bf16 [n][p], 16 KB
-constexpr uint32_t OFF_MISC = OFF_ST + NT_ * PT * 2;
 constexpr uint32_t MISC_BYTES = 2560;
-constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;   // bytes used from the 1024-aligned base
 constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
+constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192;   // Y/Yi buffer b at +128*b
 
-enum Bar { FULL0, FULL1, EMPTY0, EMPTY1, B_CB, CB_FREE, XS_FULL, S_FULL, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0,
-           Y_FREE1, DA_READY0, DA_READY1, DA_FREE0, DA_FREE1, L_FREE, OUT_READ, DRAIN, NBARS };
+// Layout for state dim NT (128 or 256).  C and B stream through a 2-stage ring in 128-column
+// halves (one half per stage), x through its own ring.  Shared memory (from a 1024-aligned
+// base): CB ring | x ring | scores 32 KB | xs 16 KB | bf16 state [n][p] | misc.
+// TMEM columns: CB 128 | Y, Yi (x YB buffers) | f32 state (64 per half) | L (64 per half).
+template <int NT>
+struct Geo {
+  static constexpr int NH = NT / 128;               // 128-column halves of the state dim
+  static constexpr int XST = NH == 1 ? 2 : 1;       // x buffers
+  static constexpr int YB = NH == 1 ? 2 : 1;        // Y/Yi accumulator buffers
+  static constexpr uint32_t SZ_H = QI * 128 * 2;    // one half of C or B: 32 KB (two 64-col boxes)
+  static constexpr uint32_t SZ_CBST = 2 * SZ_H;     // ring stage: C half + B half
+  static constexpr uint32_t SZ_X = QI * PT * 2;     // 16 KB
+  static constexpr uint32_t OFF_CB = 0;
+  static constexpr uint32_t OFF_X = 2 * SZ_CBST;
+  static constexpr uint32_t OFF_S = OFF_X + XST * SZ_X;
+  static constexpr uint32_t OFF_XS = OFF_S + QI * QI * 2;
+  static constexpr uint32_t OFF_ST = OFF_XS + SZ_X;
+  static constexpr uint32_t OFF_MISC = OFF_ST + NT * PT * 2;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
+  static constexpr uint32_t COL_ST = 128 + 128 * YB;
+  static constexpr uint32_t COL_L = COL_ST + 64 * NH;
+  static_assert(SMEM_BYTES <= SMEM_LAUNCH_BYTES, "shared memory");
+  static_assert(COL_L + 64 * NH <= TMEM_COLS, "tensor memory");
+};
+
+enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB, CB_FREE,
+           XS_FULL, S_FULL, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0, Y_FREE1, DA_READY0, DA_READY1, DA_FREE0,
+           DA_FREE1, L_FREE, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t EMPTY_COUNT = 1 + 4 + 4;   // MMA commit, SA warps (xs), SB warps (D x)
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA commit, SA warps (xs), SB warps (D x)
 constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
   uint64_t bar[NBARS];
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
   float dt[2][QI];      // processed dt
-  float red_p;          // prep: warp 2's chunk total for warp 3
   float Dv[PT];         // skip coefficient per head-dim column (0 without D)
   uint32_t tmem_base;
   volatile int abort;
@@ -106,16 +119,23 @@ struct TcArgs {
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
-// Debug trace: globaltimer at phase boundaries of CTA 0, slot [role][chunk][phase].
+// Debug trace: globaltimer at phase boundaries of CTA 0, slot [role][chunk][phase].  Compiled
+// in only with -DSSD_TC_DEBUG_TRACE (and then enabled at run time by SSD_TC_TRACE=1).
+#ifdef SSD_TC_DEBUG_TRACE
 #define TRACE(role, c, ph)                                                                       \
   do {                                                                                           \
     if (a.trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (c) < 64)                      \
       a.trace[((role) * 64 + (c)) * 16 + (ph)] = ptx::globaltimer();                             \
   } while (0)
+#else
+#define TRACE(role, c, ph) \
+  do {                     \
+  } while (0)
+#endif
 
-constexpr unsigned TIMEOUT_NS = 2000000000u;  // 2 s; a normal launch takes well under 1 ms
-// The same bound in SM clock cycles (about 2 s at the B200's 1.97 GHz boost clock): the
-// cycle counter is cheap to read, the global timer is not.
+// Wait bound in SM clock cycles: about 2 s at the B200's 1.97 GHz boost clock, where a
+// normal launch takes well under 1 ms.  The cycle counter is cheap to read, the global
+// timer is not.
 constexpr long long TIMEOUT_CYCLES = 4000000000LL;
 
 // Bounded wait.  Returns false (after flagging the CTA and the status word) on timeout or
@@ -147,37 +167,51 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 }
 
 // ---------------------------------------------------------------------------
-// producer (warp 0, lane 0): C, B, x tiles of each chunk into a 2-stage ring
+// producer (warp 0, lane 0): per chunk, the C and B columns of the head's group in
+// 128-column halves through a 2-stage ring, and the chunk's x tile through its own ring
 // ---------------------------------------------------------------------------
+template <int NT>
 __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int g) {
-  const uint32_t bytes = SZ_STAGE;
-  int c = 0;
-  for (; c < a.nci; ++c) {
-    const int s = c & 1;
-    if (c >= 2 && !wait_bar(m, EMPTY0 + s, ((c >> 1) - 1) & 1, a.status)) break;
-    uint8_t* st = sm + OFF_STAGE + s * SZ_STAGE;
-    uint64_t* full = &m->bar[FULL0 + s];
-    ptx::mbar_arrive_expect_tx(full, bytes);
+  using G_ = Geo<NT>;
+  int k = 0, c = 0;
+  bool ok = true;
+  for (; c < a.nci && ok; ++c) {
     const int t0 = c * QI;
-    ptx::tma_load_3d(st, &a.tm_c, full, g * NT_, t0, bi);
-    ptx::tma_load_3d(st + SZ_C / 2, &a.tm_c, full, g * NT_ + 64, t0, bi);
-    ptx::tma_load_3d(st + SZ_C, &a.tm_b, full, g * NT_, t0, bi);
-    ptx::tma_load_3d(st + SZ_C + SZ_C / 2, &a.tm_b, full, g * NT_ + 64, t0, bi);
-    ptx::tma_load_3d(st + 2 * SZ_C, &a.tm_x, full, h * PT, t0, bi);
+    for (int hh = 0; hh < G_::NH; ++hh, ++k) {
+      const int s = k & 1;
+      if (k >= 2 && !(ok = wait_bar(m, CB_EMPTY0 + s, ((k >> 1) - 1) & 1, a.status))) break;
+      uint8_t* st = sm + G_::OFF_CB + s * G_::SZ_CBST;
+      uint64_t* full = &m->bar[CB_FULL0 + s];
+      ptx::mbar_arrive_expect_tx(full, G_::SZ_CBST);
+      const int col = g * NT + hh * 128;
+      ptx::tma_load_3d(st, &a.tm_c, full, col, t0, bi);
+      ptx::tma_load_3d(st + G_::SZ_H / 2, &a.tm_c, full, col + 64, t0, bi);
+      ptx::tma_load_3d(st + G_::SZ_H, &a.tm_b, full, col, t0, bi);
+      ptx::tma_load_3d(st + G_::SZ_H + G_::SZ_H / 2, &a.tm_b, full, col + 64, t0, bi);
+    }
+    if (!ok) break;
+    const int xb = c % G_::XST;
+    if (c >= G_::XST && !(ok = wait_bar(m, X_EMPTY0 + xb, ((c / G_::XST) - 1) & 1, a.status))) break;
+    ptx::mbar_arrive_expect_tx(&m->bar[X_FULL0 + xb], G_::SZ_X);
+    ptx::tma_load_3d(sm + G_::OFF_X + xb * G_::SZ_X, &a.tm_x, &m->bar[X_FULL0 + xb], h * PT, t0, bi);
   }
   // drain: never leave the CTA with bulk copies still landing in its shared memory
-  for (int k = (c >= 2 ? c - 2 : 0); k < c; ++k) {
-    const int s = k & 1;
-    const uint64_t t0 = ptx::globaltimer();
-    while (!ptx::mbar_try_wait(&m->bar[FULL0 + s], (k >> 1) & 1) && ptx::globaltimer() - t0 < TIMEOUT_NS) {
+  const long long t0 = clock64();
+  for (int kk = (k >= 2 ? k - 2 : 0); kk < k; ++kk)
+    while (!ptx::mbar_try_wait(&m->bar[CB_FULL0 + (kk & 1)], (kk >> 1) & 1) && clock64() - t0 < TIMEOUT_CYCLES) {
     }
-  }
+  for (int cc = (c >= G_::XST ? c - G_::XST : 0); cc < c; ++cc)
+    while (!ptx::mbar_try_wait(&m->bar[X_FULL0 + cc % G_::XST], (cc / G_::XST) & 1) &&
+           clock64() - t0 < TIMEOUT_CYCLES) {
+    }
 }
 
 // ---------------------------------------------------------------------------
 // MMA issuer (warp 1, lane 0)
 // ---------------------------------------------------------------------------
+template <int NT>
 __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
+  using G_ = Geo<NT>;
   const uint32_t tmem = m->tmem_base;
   const uint32_t base = ptx::smem_u32(sm);
   constexpr uint32_t ID_CB = ptx::idesc_bf16_f32(128, 128, 0, 0);
@@ -185,59 +219,74 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
   constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
   for (int c = 0; c < a.nci; ++c) {
-    const int s = c & 1, yb = c & 1;
-    const uint32_t st = base + OFF_STAGE + s * SZ_STAGE;
-    const uint32_t sC = st, sB = st + SZ_C, sX = st + 2 * SZ_C;
-    // MMA1: CB = C . B^T (both K-major: row = token, K = state dim in two 64-wide boxes)
-    if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) break;
-    if (c > 0 && !wait_bar(m, CB_FREE, (c - 1) & 1, a.status)) break;
-    ptx::tc_fence_after();
+    const int yb = c % G_::YB, xb = c % G_::XST;
+    const uint32_t colY = COL_Y0 + 128 * yb, colYI = COL_YI0 + 128 * yb;
+    // MMA1: CB = C . B^T, summed over the 128-column halves of the state dim (K-major)
+    for (int hh = 0; hh < G_::NH; ++hh) {
+      const int k = c * G_::NH + hh;
+      if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) goto drain;
+      if (hh == 0 && c > 0 && !wait_bar(m, CB_FREE, (c - 1) & 1, a.status)) goto drain;
+      ptx::tc_fence_after();
+      const uint32_t sC = base + G_::OFF_CB + (k & 1) * G_::SZ_CBST, sB = sC + G_::SZ_H;
 #pragma unroll
-    for (int i = 0; i < NT_ / 16; ++i) {
-      const uint32_t off = (i >> 2) * (SZ_C / 2) + (i & 3) * 32;
-      ptx::mma_f16(tmem + COL_CB, ptx::sdesc_sw128(sC + off, 16, 1024), ptx::sdesc_sw128(sB + off, 16, 1024),
-                   ID_CB, i > 0);
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t off = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
+        ptx::mma_f16(tmem + COL_CB, ptx::sdesc_sw128(sC + off, 16, 1024), ptx::sdesc_sw128(sB + off, 16, 1024),
+                     ID_CB, (hh > 0 || i > 0) ? 1u : 0u);
+      }
     }
     ptx::mma_commit(&m->bar[B_CB]);
     TRACE(4, c, 0);
-    // MMA3: Yi[yb] = C . S_c^T   (B operand = bf16 state [n][p], MN-major)  -- the state chain
-    if (!wait_bar(m, ST_READY, c & 1, a.status)) break;
-    if (c >= 2 && !wait_bar(m, Y_FREE0 + yb, ((c - 2) >> 1) & 1, a.status)) break;
+    // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)  -- the state chain
+    if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
+    if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
+    for (int hh = 0; hh < G_::NH; ++hh) {
+      const uint32_t sC = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST;
 #pragma unroll
-    for (int i = 0; i < NT_ / 16; ++i) {
-      const uint32_t offa = (i >> 2) * (SZ_C / 2) + (i & 3) * 32;
-      ptx::mma_f16(tmem + COL_YI0 + 128 * yb, ptx::sdesc_sw128(sC + offa, 16, 1024),
-                   ptx::sdesc_sw128(base + OFF_ST + i * 2048, 8192, 1024), ID_YI, i > 0);
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t offa = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
+        ptx::mma_f16(tmem + colYI, ptx::sdesc_sw128(sC + offa, 16, 1024),
+                     ptx::sdesc_sw128(base + G_::OFF_ST + hh * (128 * 128) + i * 2048, 8192, 1024), ID_YI,
+                     (hh > 0 || i > 0) ? 1u : 0u);
+      }
     }
-    // MMA_L: Lt = B^T . xs   (A = B tile read MN-major, B = xs [t][p] MN-major)
-    if (!wait_bar(m, XS_FULL, c & 1, a.status)) break;
-    if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) break;
+    // MMA_L: L_c = B^T . xs, one 128-row half of the state dim per ring stage
+    if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
+    if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
+    for (int hh = 0; hh < G_::NH; ++hh) {
+      const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
 #pragma unroll
-    for (int i = 0; i < QI / 16; ++i) {
-      ptx::mma_f16(tmem + COL_L, ptx::sdesc_sw128(sB + i * 2048, SZ_C / 2, 1024),
-                   ptx::sdesc_sw128(base + OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
+      for (int i = 0; i < QI / 16; ++i)
+        ptx::mma_f16(tmem + G_::COL_L + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
+                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
     }
-    ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state and MMA_L(c) with xs
+    for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
+    ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
     TRACE(4, c, 1);
-    // MMA2: Y[yb] = S . x   (A = scores K-major, B = x [t][p] MN-major)
-    if (!wait_bar(m, S_FULL, c & 1, a.status)) break;
+    // MMA2: Y = S . x   (A = scores K-major, B = x [t][p] MN-major)
+    if (!wait_bar(m, S_FULL, c & 1, a.status)) goto drain;
+    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
+    {
+      const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
-    for (int i = 0; i < QI / 16; ++i) {
-      const uint32_t offa = (i >> 2) * (QI * 128) + (i & 3) * 32;
-      ptx::mma_f16(tmem + COL_Y0 + 128 * yb, ptx::sdesc_sw128(base + OFF_S + offa, 16, 1024),
-                   ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
+      for (int i = 0; i < QI / 16; ++i) {
+        const uint32_t offa = (i >> 2) * (QI * 128) + (i & 3) * 32;
+        ptx::mma_f16(tmem + colY, ptx::sdesc_sw128(base + G_::OFF_S + offa, 16, 1024),
+                     ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
+      }
     }
     ptx::mma_commit(&m->bar[B_Y0 + yb]);
-    ptx::mma_commit(&m->bar[EMPTY0 + s]);
+    ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
     TRACE(4, c, 2);
   }
-  // drain: wait (bounded) until every issued MMA has completed
+drain:
+  // wait (bounded) until every issued MMA has completed
   ptx::mma_commit(&m->bar[DRAIN]);
-  const uint64_t t0 = ptx::globaltimer();
-  while (!ptx::mbar_try_wait(&m->bar[DRAIN], 0) && ptx::globaltimer() - t0 < TIMEOUT_NS) {
+  const long long t0 = clock64();
+  while (!ptx::mbar_try_wait(&m->bar[DRAIN], 0) && clock64() - t0 < TIMEOUT_CYCLES) {
   }
 }
 
@@ -276,41 +325,39 @@ __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
   return o;
 }
 
-__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
-  return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
-}
-
 // ---------------------------------------------------------------------------
-// prep (warps 2-3): processed dt and in-chunk cumulative dA into the shared arrays
-// (double-buffered by chunk parity).  Thread j of the 64 owns rows 2j and 2j+1.
+// prep (warp 2): processed dt and in-chunk cumulative dA into the shared arrays
+// (double-buffered by chunk parity).  Lane l owns rows 4l..4l+3; one warp, so no
+// cross-warp barrier is needed.
 // ---------------------------------------------------------------------------
 __device__ void prep_worker(const TcArgs& a, Misc* m, int bi, int h) {
-  const int j = threadIdx.x - 64;          // 0..63
-  const int lane = j & 31, w = j >> 5;     // w: 0 -> rows 0..63, 1 -> rows 64..127
-  const int r0 = 2 * j, r1 = 2 * j + 1;
+  const int lane = threadIdx.x & 31;
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  ChunkDt n0 = load_dt(a, bi, h, 0, r0), n1 = load_dt(a, bi, h, 0, r1);
+  ChunkDt nx[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) nx[i] = load_dt(a, bi, h, 0, 4 * lane + i);
 #pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
     const int buf = c & 1;
     const int64_t t0 = (int64_t)c * QI;
-    const ChunkDt c0 = n0, c1 = n1;
-    n0 = load_dt(a, bi, h, c + 1, r0);
-    n1 = load_dt(a, bi, h, c + 1, r1);
-    const float d0 = (t0 + r0 < a.L) ? dt_process(c0.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-    const float d1 = (t0 + r1 < a.L) ? dt_process(c1.raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-    float cs = warp_incl_scan((d0 + d1) * Ah);
+    float d[4], run = 0.f, cs[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      d[i] = (t0 + 4 * lane + i < a.L) ? dt_process(nx[i].raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+      run += d[i] * Ah;
+      cs[i] = run;
+      nx[i] = load_dt(a, bi, h, c + 1, 4 * lane + i);
+    }
+    const float excl = warp_incl_scan(run) - run;
     // the arrays of chunk c-2 (same buffer) must be released by every reader
     if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) return;
-    if (w == 0 && lane == 31) m->red_p = cs;
-    ptx::named_bar_sync(1, 64);
-    if (w == 1) cs += m->red_p;
-    m->dA[buf][r0] = cs - d1 * Ah;
-    m->dA[buf][r1] = cs;
-    m->dt[buf][r0] = d0;
-    m->dt[buf][r1] = d1;
-    ptx::named_bar_sync(1, 64);   // also keeps red_p from being overwritten early
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      m->dA[buf][4 * lane + i] = cs[i] + excl;
+      m->dt[buf][4 * lane + i] = d[i];
+    }
+    __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&m->bar[DA_READY0 + buf]);
   }
 }
@@ -319,20 +366,21 @@ __device__ void prep_worker(const TcArgs& a, Misc* m, int bi, int h) {
 // staged as f32 in the (free) score buffer as two 128B-swizzled [128][32] boxes and
 // written by one TMA bulk store per box, so global writes are full lines.  The inner
 // loops carry no data-dependent branches (each costs tens of cycles when unrolled).
-template <bool HAS_Z>
+template <int NT, bool HAS_Z>
 __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tmem, int bi, int h, int c, int r,
                              float sdec) {
-  const int yb = c & 1, s = c & 1;
+  using G_ = Geo<NT>;
+  const int yb = c % G_::YB, xb = c % G_::XST;
   const int lane = r & 31;
   const int64_t pos = (int64_t)c * QI + r;
   const bool valid = pos < a.L;
   const int64_t o0 = (((int64_t)bi * a.L + (valid ? pos : 0)) * a.H + h) * PT;
   float* const out_x = a.out_x;
   const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
-  if (!wait_bar(m, B_Y0 + yb, (c >> 1) & 1, a.status)) return false;   // also: MMA2(c) done with S
+  if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;   // also: MMA2(c) done with S
   ptx::tc_fence_after();
-  const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
-  uint8_t* stage = sm + OFF_S;
+  const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
+  uint8_t* stage = sm + G_::OFF_S;
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float y[32], yi[32];
@@ -380,18 +428,22 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   __syncwarp();
   if (lane == 0) {
     ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
-    ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
   }
-  ptx::named_bar_sync(2, 128);                 // all 128 rows staged
+  if (r == 0) TRACE(1, c, 5);
+  if (lane == 0) ptx::mbar_arrive(&m->bar[STAGED]);
   if (r == 0) {
+    // all 128 rows staged: one bulk store per 32-column box
+    if (!wait_bar(m, STAGED, c & 1, a.status)) return false;
     ptx::tma_store_3d(&a.tm_out, stage, h * PT, c * QI, bi);
     ptx::tma_store_3d(&a.tm_out, stage + QI * 128, h * PT + 32, c * QI, bi);
     ptx::bulk_commit();
     ptx::bulk_wait_read();                     // staging buffer read: score buffer free again
     ptx::mbar_arrive(&m->bar[OUT_READ]);
   }
-  ptx::named_bar_sync(2, 128);
-  return true;
+  const bool ok = wait_bar(m, OUT_READ, c & 1, a.status);
+  if (r == 0) TRACE(1, c, 6);
+  return ok;
 }
 
 // One 32-column block of scores for row r: v[i] holds CB[r][t] (t = 32*k32 + i) on entry.
@@ -403,7 +455,11 @@ __device__ __forceinline__ void score_block(float (&v)[32], float u, float vl, f
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     bool ok = !DIAG || i <= lane;
-    if (HAS_SEQ) ok = ok && (__shfl_sync(0xffffffffu, sl, i) == seqv);
+    if (HAS_SEQ) {
+      // every lane takes part in the shuffle (a short-circuited __shfl_sync would diverge)
+      const int st = __shfl_sync(0xffffffffu, sl, i);
+      ok = ok && (st == seqv);
+    }
     if (FAC) {
       const float w = u * __shfl_sync(0xffffffffu, vl, i);
       v[i] = ok ? v[i] * w : 0.f;
@@ -419,7 +475,7 @@ __device__ __forceinline__ void score_block(float (&v)[32], float u, float vl, f
 // blocks, so no warp does more than two).  SA also builds xs; SB first writes the output
 // of the previous chunk.
 // ---------------------------------------------------------------------------
-template <bool HAS_SEQ, bool HAS_Z>
+template <int NT, bool HAS_SEQ, bool HAS_Z>
 __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int half) {
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
@@ -430,14 +486,16 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   // non-increasing (A <= 0, dt >= 0); otherwise every element is formed directly.
   const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
   constexpr bool has_seq = HAS_SEQ;
-  uint8_t* S_sm = sm + OFF_S;
-  uint8_t* xs_sm = sm + OFF_XS;
+  using G_ = Geo<NT>;
+  uint8_t* S_sm = sm + G_::OFF_S;
+  uint8_t* xs_sm = sm + G_::OFF_XS;
   float sdec_prev = 0.f;
 #pragma unroll 1
   for (int c = 0; c < a.nci; ++c) {
-    const int buf = c & 1, s = c & 1;
+    const int buf = c & 1, xb = c % G_::XST;
     const int64_t t0 = (int64_t)c * QI;
-    if (half == 1 && c > 0 && !output_chunk<HAS_Z>(a, sm, m, tmem, bi, h, c - 1, r, sdec_prev)) return;
+    if (r == 0) TRACE(half, c, 0);
+    if (half == 1 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, c - 1, r, sdec_prev)) return;
     int seqv = (t0 + r < a.L) ? 0 : -1, prev_seq = 0, end_seq = 0, sl0 = 0, sl1 = 0;
     const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
     if (has_seq) {
@@ -448,14 +506,15 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
     }
     if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
+    if (r == 0) TRACE(half, c, 1);
     const float dA = m->dA[buf][r];
 
     if (half == 0) {
       // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
       const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(m->dA[buf][QI - 1] - dA) * m->dt[buf][r] : 0.f;
-      if (!wait_bar(m, FULL0 + s, (c >> 1) & 1, a.status)) return;
+      if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
       if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
-      const uint8_t* x_sm = sm + OFF_STAGE + s * SZ_STAGE + 2 * SZ_C;
+      const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
         *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, k)) =
@@ -464,7 +523,7 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       __syncwarp();
       if (lane == 0) {
         ptx::mbar_arrive(&m->bar[XS_FULL]);
-        ptx::mbar_arrive(&m->bar[EMPTY0 + s]);
+        ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
       }
       // the score buffer still holds the previous chunk's staged output until its bulk
       // store has read it
@@ -522,33 +581,38 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     if ((r == 0 || r == 96) && half == 0) TRACE(r == 0 ? 0 : 1, c, 8);
   }
   if (half == 1 && a.nci > 0) {
-    if (!output_chunk<HAS_Z>(a, sm, m, tmem, bi, h, a.nci - 1, r, sdec_prev)) return;
+    if (!output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, a.nci - 1, r, sdec_prev)) return;
     if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
   }
 }
 
 // ---------------------------------------------------------------------------
 // state worker T (warps 12-15): S_{c+1} = keep_c exp(dA_last_c) S_c + L_c.  Thread r owns
-// state row n = r (TMEM lane r): 64 f32 columns of the state and of L_c.
+// state rows n = r + 128*hh (TMEM lane r, 64 f32 columns per 128-row half) of the state
+// and of L_c.
 // ---------------------------------------------------------------------------
+template <int NT>
 __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
+  using G_ = Geo<NT>;
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
-  uint8_t* st_sm = sm + OFF_ST;
+  uint8_t* st_sm = sm + G_::OFF_ST;
   const int64_t bh = (int64_t)bi * a.H + h;
   // S_0 = initial state (or 0): f32 in TMEM, bf16 operand for MMA3(0)
 #pragma unroll 1
-  for (int half = 0; half < 2; ++half) {
+  for (int seg = 0; seg < 2 * G_::NH; ++seg) {
+    const int hh = seg >> 1, half = seg & 1;
+    const int n = hh * 128 + r;
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = a.init ? a.init[(bh * PT + 32 * half + i) * NT_ + r] : 0.f;
+    for (int i = 0; i < 32; ++i) v[i] = a.init ? a.init[(bh * PT + 32 * half + i) * NT + n] : 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, 4 * half + j)) =
+      *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
           make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                      pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
-    ptx::tmem_st32(tl + COL_ST + 32 * half, v);
+    ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, v);
   }
   ptx::tmem_st_wait();
   ptx::tc_fence_before();
@@ -572,28 +636,30 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     const float decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
     prev_end = end_seq;
-    if (r == 0) TRACE(2, c, 0);
+    TRACE(2, c, 0);
     if (!wait_bar(m, B_L, c & 1, a.status)) return;   // L_c ready, MMA3(c) done with S_c
-    if (r == 0) TRACE(2, c, 1);
+    TRACE(2, c, 1);
     ptx::tc_fence_after();
 #pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
+    for (int seg = 0; seg < 2 * G_::NH; ++seg) {
+      const int hh = seg >> 1, half = seg & 1;
+      const int n = hh * 128 + r;
       float sv[32], lv[32];
-      ptx::tmem_ld32(tl + COL_ST + 32 * half, sv);
-      ptx::tmem_ld32(tl + COL_L + 32 * half, lv);
+      ptx::tmem_ld32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
+      ptx::tmem_ld32(tl + G_::COL_L + 64 * hh + 32 * half, lv);
       ptx::tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 32; ++i) sv[i] = decay * sv[i] + lv[i];
       if (more) {
-        ptx::tmem_st32(tl + COL_ST + 32 * half, sv);
+        ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(r, 4 * half + j)) =
+          *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
               make_uint4(pack_bf16(sv[8 * j], sv[8 * j + 1]), pack_bf16(sv[8 * j + 2], sv[8 * j + 3]),
                          pack_bf16(sv[8 * j + 4], sv[8 * j + 5]), pack_bf16(sv[8 * j + 6], sv[8 * j + 7]));
       } else if (a.final_states) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a.final_states[(bh * PT + 32 * half + i) * NT_ + r] = sv[i];
+        for (int i = 0; i < 32; ++i) a.final_states[(bh * PT + 32 * half + i) * NT + n] = sv[i];
       }
     }
     if (more) ptx::tmem_st_wait();
@@ -604,32 +670,37 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       ptx::mbar_arrive(&m->bar[L_FREE]);
       if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
     }
-    if (r == 0) TRACE(2, c, 2);
+    TRACE(2, c, 2);
   }
 }
 
-template <bool HAS_SEQ, bool HAS_Z>
+template <int NT, bool HAS_SEQ, bool HAS_Z>
 __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // Align by pointer arithmetic on the shared array itself (not through an integer cast)
   // so that every access below stays a shared-space load/store.
   uint8_t* sm = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
-  if (sm - smem_raw > (ptrdiff_t)(SMEM_LAUNCH_BYTES - SMEM_BYTES)) {
+  using G_ = Geo<NT>;
+  if (sm - smem_raw > (ptrdiff_t)(SMEM_LAUNCH_BYTES - G_::SMEM_BYTES)) {
     // the dynamic shared window is not aligned enough for the swizzled tiles: report, do nothing
     if (threadIdx.x == 0) atomicCAS(a.status, 0u, 0x200u);
     return;
   }
-  Misc* m = reinterpret_cast<Misc*>(sm + OFF_MISC);
+  Misc* m = reinterpret_cast<Misc*>(sm + G_::OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
   const int bi = bh / a.H, h = bh % a.H;
   const int g = h / (a.H / a.G);
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(&m->bar[FULL0], 1);
-    ptx::mbar_init(&m->bar[FULL1], 1);
-    ptx::mbar_init(&m->bar[EMPTY0], EMPTY_COUNT);
-    ptx::mbar_init(&m->bar[EMPTY1], EMPTY_COUNT);
+    ptx::mbar_init(&m->bar[CB_FULL0], 1);
+    ptx::mbar_init(&m->bar[CB_FULL1], 1);
+    ptx::mbar_init(&m->bar[CB_EMPTY0], 1);
+    ptx::mbar_init(&m->bar[CB_EMPTY1], 1);
+    ptx::mbar_init(&m->bar[X_FULL0], 1);
+    ptx::mbar_init(&m->bar[X_FULL1], 1);
+    ptx::mbar_init(&m->bar[X_EMPTY0], X_EMPTY_COUNT);
+    ptx::mbar_init(&m->bar[X_EMPTY1], X_EMPTY_COUNT);
     ptx::mbar_init(&m->bar[B_CB], 1);
     ptx::mbar_init(&m->bar[CB_FREE], 8);
     ptx::mbar_init(&m->bar[XS_FULL], 4);
@@ -640,11 +711,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[B_Y1], 1);
     ptx::mbar_init(&m->bar[Y_FREE0], 4);
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
-    ptx::mbar_init(&m->bar[DA_READY0], 2);
-    ptx::mbar_init(&m->bar[DA_READY1], 2);
+    ptx::mbar_init(&m->bar[DA_READY0], 1);
+    ptx::mbar_init(&m->bar[DA_READY1], 1);
     ptx::mbar_init(&m->bar[DA_FREE0], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[DA_FREE1], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[L_FREE], 4);
+    ptx::mbar_init(&m->bar[STAGED], 4);
     ptx::mbar_init(&m->bar[OUT_READ], 1);
     ptx::mbar_init(&m->bar[DRAIN], 1);
     m->abort = 0;
@@ -667,15 +739,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   ptx::tc_fence_after();
 
   if (warp == 0) {
-    if (lane == 0) producer(a, sm, m, bi, h, g);
+    if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
   } else if (warp == 1) {
-    if (lane == 0) mma_issuer(a, sm, m);
-  } else if (warp < 4) {
+    if (lane == 0) mma_issuer<NT>(a, sm, m);
+  } else if (warp == 2) {
     prep_worker(a, m, bi, h);
+  } else if (warp == 3) {
+    // spare warp
   } else if (warp < 12) {
-    score_worker<HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
+    score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
   } else {
-    state_worker(a, sm, m, bi, h);
+    state_worker<NT>(a, sm, m, bi, h);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -723,7 +797,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint6
 }  // namespace
 
 bool tc_supported(const ssd_fwd_params_t* p) {
-  if (p->dtype != SSD_DTYPE_BF16 || p->headdim != PT || p->dstate != NT_) return false;
+  if (p->dtype != SSD_DTYPE_BF16 || p->headdim != PT || (p->dstate != 128 && p->dstate != 256)) return false;
   if (p->dA_cumsum || p->dt_out || p->varlen_states) return false;
   if (p->batch * p->nheads > 0x7fffffff) return false;
   const uintptr_t al = 15;
@@ -735,6 +809,9 @@ bool tc_supported(const ssd_fwd_params_t* p) {
 }
 
 bool trace_enabled() {
+#ifndef SSD_TC_DEBUG_TRACE
+  return false;
+#endif
   static int on = -1;
   if (on < 0) {
     const char* e = getenv("SSD_TC_TRACE");
@@ -754,8 +831,8 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   TcArgs a;
   memset(&a, 0, sizeof(a));
   const int64_t b = p->batch, L = p->seqlen, H = p->nheads, G = p->ngroups;
-  if (!make_map(&a.tm_x, p->x, (uint64_t)H * PT, L, b) || !make_map(&a.tm_b, p->B, (uint64_t)G * NT_, L, b) ||
-      !make_map(&a.tm_c, p->C, (uint64_t)G * NT_, L, b) ||
+  if (!make_map(&a.tm_x, p->x, (uint64_t)H * PT, L, b) || !make_map(&a.tm_b, p->B, (uint64_t)G * p->dstate, L, b) ||
+      !make_map(&a.tm_c, p->C, (uint64_t)G * p->dstate, L, b) ||
       !make_map(&a.tm_out, p->out, (uint64_t)H * PT, L, b, true)) {
     set_last_error("cuTensorMapEncodeTiled failed for x/B/C/out");
     return SSD_ERR_CUDA;
@@ -769,10 +846,13 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.status = (unsigned*)workspace;
   a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256) : nullptr;
   typedef void (*KernelFn)(TcArgs);
-  static const KernelFn kernels[4] = {ssd_fused_tc_kernel<false, false>, ssd_fused_tc_kernel<false, true>,
-                                      ssd_fused_tc_kernel<true, false>, ssd_fused_tc_kernel<true, true>};
-  static bool attr[4] = {false, false, false, false};
-  const int kid = (p->seq_idx ? 2 : 0) + (p->z ? 1 : 0);
+  static const KernelFn kernels[8] = {
+      ssd_fused_tc_kernel<128, false, false>, ssd_fused_tc_kernel<128, false, true>,
+      ssd_fused_tc_kernel<128, true, false>,  ssd_fused_tc_kernel<128, true, true>,
+      ssd_fused_tc_kernel<256, false, false>, ssd_fused_tc_kernel<256, false, true>,
+      ssd_fused_tc_kernel<256, true, false>,  ssd_fused_tc_kernel<256, true, true>};
+  static bool attr[8] = {false, false, false, false, false, false, false, false};
+  const int kid = (p->dstate == 256 ? 4 : 0) + (p->seq_idx ? 2 : 0) + (p->z ? 1 : 0);
   const KernelFn kern = kernels[kid];
   if (!attr[kid]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) != cudaSuccess) {

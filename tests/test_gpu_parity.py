@@ -329,3 +329,31 @@ def test_tensor_core_path_selected():
         torch.cuda.synchronize()
         if want:
             assert int(r.workspace[:4].view(torch.int32).item()) == 0  # device status word
+
+
+@pytest.mark.parametrize("N,lens", [(256, None), (256, [100, 300, 7, 233]), (128, [128, 1, 300, 211])],
+                         ids=["n256", "n256-seq", "n128-seq"])
+@pytest.mark.parametrize("z", [False, True])
+def test_tensor_core_path_state_dims_and_seq_idx(N, lens, z):
+    """The fused tcgen05 kernel at N=128 and N=256, with packed seq_idx (no varlen states
+    requested, so the tensor-core path runs)."""
+    from mamba2_b200 import mamba_chunk_scan_combined_fwd
+    from mamba2_b200.runner import SsdForward
+    L = 640 if lens is None else sum(lens)
+    cfg = S.SsdConfig("t", 1 if lens else 2, L, 8, 64, 2, N, 128, "bf16", has_z=z, has_init=True,
+                      return_final=True)
+    inp = S.make_ssd_inputs(cfg, 31 + N)
+    seq = None if lens is None else np.repeat(np.arange(len(lens)), lens)[None].astype(np.int32)
+    d = dev_inputs(inp, "bf16")
+    sd = to_dev(seq, int32=True)
+    r = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 128, D=d["D"], z=d["z"], dt_bias=d["dt_bias"],
+                   initial_states=d["initial_states"], seq_idx=sd, dt_softplus=True, return_final_states=True)
+    assert r.uses_tc
+    out = r()
+    torch.cuda.synchronize()
+    assert int(r.workspace[:4].view(torch.int32).item()) == 0
+    ref_out, ref_final = R.ssd_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], 128, D=inp["D"],
+                                        z=inp["z"], dt_bias=inp["dt_bias"], initial_states=inp["initial_states"],
+                                        seq_idx=seq, dt_softplus=True, return_final_states=True)
+    assert rel_l2(out, ref_out) <= TOL["bf16"]
+    assert rel_l2(r.final, ref_final) <= TOL["bf16"]
