@@ -9,7 +9,7 @@
 //
 // Per chunk c (t = token in chunk, m = output row, n = state dim, p = head dim):
 //   MMA1  CB[m][t]  = C[m][:] . B[t][:]                 (M=128, N=128, K=N)   TMEM
-//   E2    S[m][t]   = CB[m][t] exp(dA_m - dA_t) dt_t    (t <= m, same seq)    -> smem bf16
+//   E2    S[m][t]   = CB[m][t] exp(dA_m - dA_t) dt_t    (t <= m, same seq)    -> TMEM bf16
 //   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM (2 bufs)
 //   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM (2 bufs)
 //   E1    xs[t][p]  = x[t][p] exp(dA_last - dA_t) dt_t  (chunk-end seq only)  -> smem bf16
@@ -26,11 +26,12 @@
 //   warp 1      MMA issuer (lane 0); owns the TMEM allocation (all 512 columns)
 //   warp 2      prep: processed dt and cumulative dA of each chunk (shared arrays); warp 3 spare
 //   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
-//   warps 8-11  SB: output epilogue E4 of the previous chunk (staged through the free score
-//               buffer and written by a TMA bulk store), then score column blocks 1 and 3
+//   warps 8-11  SB: output epilogue E4 of the previous chunk (staged in shared memory and
+//               written by a TMA bulk store), then score column blocks 1 and 3
 //   warps 12-15 T: the state recurrence E3
 // MMA_L accumulates the chunk's state contribution L_c in its own TMEM columns, so xs and
-// MMA_L do not wait for the state chain.  Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk
+// MMA_L do not wait for the state chain.  The bf16 scores go back into TMEM (over the CB
+// columns already read) and MMA2 takes them from there as its A operand.  Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk
 // rows of its quadrant; TMEM reads are issued 32 columns at a time with one wait, since
 // each round trip is expensive.
 // Every mbarrier wait is bounded; on timeout the CTA records SSD_ERR_TIMEOUT in the status
@@ -95,6 +96,7 @@ struct Misc {
   float dt[2][QI];      // processed dt
   float Dv[PT];         // skip coefficient per head-dim column (0 without D)
   uint32_t tmem_base;
+  int nci;              // chunks of this CTA's walk (from the schedule when there is one)
   volatile int abort;
 };
 static_assert(sizeof(Misc) <= MISC_BYTES, "misc area");
@@ -115,6 +117,9 @@ struct TcArgs {
   float* out;
   float* out_x;
   float* final_states;
+  float* varlen_states;        // (num_seqs, H, P, N) or null
+  const int* sched_n;          // chunk count written by the schedule kernel, or null
+  const int2* sched;           // {t0, varlen slot or -1} per chunk, entry nci = {L, -1}
   unsigned* status;
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
@@ -166,6 +171,27 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
+// Tokens [t0, t0 + n) of chunk c.  Without a schedule the chunks tile the sequence in 128s;
+// with one (varlen states) every packed sequence is tiled from its own start, so each
+// sequence ends at a chunk end and its final state is the running state after that chunk.
+struct Span {
+  int t0, n, vslot;   // vslot: index of the sequence this chunk ends, or -1
+};
+__device__ __forceinline__ Span span_at(const TcArgs& a, int c) {
+  Span s;
+  if (a.sched) {
+    const int2 e = a.sched[c];
+    s.t0 = e.x;
+    s.vslot = e.y;
+    s.n = a.sched[c + 1].x - e.x;
+  } else {
+    s.t0 = c * QI;
+    s.n = min(QI, a.L - s.t0);
+    s.vslot = -1;
+  }
+  return s;
+}
+
 // ---------------------------------------------------------------------------
 // producer (warp 0, lane 0): per chunk, the C and B columns of the head's group in
 // 128-column halves through a 2-stage ring, and the chunk's x tile through its own ring
@@ -175,8 +201,10 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
   using G_ = Geo<NT>;
   int k = 0, c = 0;
   bool ok = true;
-  for (; c < a.nci && ok; ++c) {
-    const int t0 = c * QI;
+  const int nci = m->nci;
+  for (; c < nci && ok; ++c) {
+    const int t0 = span_at(a, c).t0;
+    TRACE(6, c, 0);
     for (int hh = 0; hh < G_::NH; ++hh, ++k) {
       const int s = k & 1;
       if (k >= 2 && !(ok = wait_bar(m, CB_EMPTY0 + s, ((k >> 1) - 1) & 1, a.status))) break;
@@ -194,6 +222,7 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
     if (c >= G_::XST && !(ok = wait_bar(m, X_EMPTY0 + xb, ((c / G_::XST) - 1) & 1, a.status))) break;
     ptx::mbar_arrive_expect_tx(&m->bar[X_FULL0 + xb], G_::SZ_X);
     ptx::tma_load_3d(sm + G_::OFF_X + xb * G_::SZ_X, &a.tm_x, &m->bar[X_FULL0 + xb], h * PT, t0, bi);
+    TRACE(6, c, 1);
   }
   // drain: never leave the CTA with bulk copies still landing in its shared memory
   const long long t0 = clock64();
@@ -218,8 +247,10 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
   constexpr uint32_t ID_YI = ptx::idesc_bf16_f32(128, 64, 0, 1);
   constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
   constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
-  for (int c = 0; c < a.nci; ++c) {
+  const int nci = m->nci;
+  for (int c = 0; c < nci; ++c) {
     const int yb = c % G_::YB, xb = c % G_::XST;
+    TRACE(4, c, 0);
     const uint32_t colY = COL_Y0 + 128 * yb, colYI = COL_YI0 + 128 * yb;
     // MMA1: CB = C . B^T, summed over the 128-column halves of the state dim (K-major)
     for (int hh = 0; hh < G_::NH; ++hh) {
@@ -236,9 +267,10 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
       }
     }
     ptx::mma_commit(&m->bar[B_CB]);
-    TRACE(4, c, 0);
+    TRACE(4, c, 1);
     // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)  -- the state chain
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
+    TRACE(4, c, 2);
     if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
@@ -254,6 +286,7 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
     // MMA_L: L_c = B^T . xs, one 128-row half of the state dim per ring stage
     if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
     if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) goto drain;
+    TRACE(4, c, 3);
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
       const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
@@ -264,23 +297,24 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
     }
     for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
     ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
-    TRACE(4, c, 1);
-    // MMA2: Y = S . x   (A = scores K-major, B = x [t][p] MN-major)
+    // MMA2: Y = S . x   (A = bf16 scores in TMEM, B = x [t][p] MN-major).  The scores of
+    // tokens 32k..32k+31 sit in the first 16 columns of CB block k; MMA1(c+1), issued after
+    // this by the same thread, overwrites them only after these reads (tcgen05.mma of one
+    // thread execute in issue order).
     if (!wait_bar(m, S_FULL, c & 1, a.status)) goto drain;
+    TRACE(4, c, 4);
     if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     {
       const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
-      for (int i = 0; i < QI / 16; ++i) {
-        const uint32_t offa = (i >> 2) * (QI * 128) + (i & 3) * 32;
-        ptx::mma_f16(tmem + colY, ptx::sdesc_sw128(base + G_::OFF_S + offa, 16, 1024),
-                     ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
-      }
+      for (int i = 0; i < QI / 16; ++i)
+        ptx::mma_f16_ts(tmem + colY, tmem + COL_CB + 32 * (i >> 1) + 8 * (i & 1),
+                        ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
     }
     ptx::mma_commit(&m->bar[B_Y0 + yb]);
     ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
-    TRACE(4, c, 2);
+    TRACE(4, c, 5);
   }
 drain:
   // wait (bounded) until every issued MMA has completed
@@ -293,21 +327,16 @@ drain:
 // ---------------------------------------------------------------------------
 // helpers shared by the worker warpgroups
 // ---------------------------------------------------------------------------
-struct ChunkDt {
-  float raw;
-  int seq;
-};
-
-// Raw dt and seq id of chunk row r (seq -1 past the end of the sequence or the chunks).
-__device__ __forceinline__ ChunkDt load_dt(const TcArgs& a, int bi, int h, int c, int r) {
-  ChunkDt d{0.f, -1};
-  const int64_t pos = (int64_t)c * QI + r;
-  if (c < a.nci && pos < a.L) {
-    const int64_t di = ((int64_t)bi * a.L + pos) * a.H + h;
-    d.raw = a.dt_bf16 ? __bfloat162float(((const bf16*)a.dt)[di]) : ((const float*)a.dt)[di];
-    d.seq = a.seq_idx ? a.seq_idx[(int64_t)bi * a.L + pos] : 0;
-  }
-  return d;
+// Raw dt of chunk row r, loaded unconditionally from a clamped (always valid) address: the
+// caller masks rows past the chunk's end when it uses the value.  A conditional load here
+// would be merged with its fallback value at once, and the merge waits for the load (a
+// few microseconds under this kernel's memory traffic), defeating the prefetch.
+template <bool DT_BF16>
+__device__ __forceinline__ float load_dt(const TcArgs& a, int bi, int h, int nci, int c, int r) {
+  const Span sp = span_at(a, min(c, nci - 1));
+  const int64_t di = ((int64_t)bi * a.L + sp.t0 + min(r, sp.n - 1)) * a.H + h;
+  if (DT_BF16) return __bfloat162float(__ldg((const bf16*)a.dt + di));
+  return __ldg((const float*)a.dt + di);
 }
 
 __device__ __forceinline__ int seq_at(const TcArgs& a, int bi, int64_t pos) {
@@ -330,35 +359,63 @@ __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
 // (double-buffered by chunk parity).  Lane l owns rows 4l..4l+3; one warp, so no
 // cross-warp barrier is needed.
 // ---------------------------------------------------------------------------
+// One chunk of prep: consumes f (raw dt of chunk c), then refills f with chunk c + 3.
+template <bool DT_BF16>
+__device__ __forceinline__ bool prep_chunk(const TcArgs& a, Misc* m, int bi, int h, int nci, int c, float Ah,
+                                           float bias, int lane, float (&f)[4]) {
+  const int buf = c & 1;
+  const int n = span_at(a, c).n;
+  TRACE(7, c, 0);
+  float d[4], run = 0.f, cs[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    d[i] = (4 * lane + i < n) ? dt_process(f[i], bias, a.softplus, a.lo, a.hi) : 0.f;
+    run += d[i] * Ah;
+    cs[i] = run;
+  }
+  TRACE(7, c, 4);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[i] = load_dt<DT_BF16>(a, bi, h, nci, c + 3, 4 * lane + i);
+  }
+  const float excl = warp_incl_scan(run) - run;
+  TRACE(7, c, 3);
+  // the arrays of chunk c-2 (same buffer) must be released by every reader
+  if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) return false;
+  TRACE(7, c, 1);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m->dA[buf][4 * lane + i] = cs[i] + excl;
+    m->dt[buf][4 * lane + i] = d[i];
+  }
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive(&m->bar[DA_READY0 + buf]);
+  TRACE(7, c, 2);
+  return true;
+}
+
+template <bool DT_BF16>
 __device__ void prep_worker(const TcArgs& a, Misc* m, int bi, int h) {
   const int lane = threadIdx.x & 31;
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  ChunkDt nx[4];
+  const int nci = m->nci;
+  if (nci <= 0) return;
+  // Raw dt (128 separate lines per chunk) is loaded three chunks before its use into one
+  // of three register sets; the loop is unrolled by three so no set is copied (a copy
+  // would wait for its load): these loads take microseconds under the kernel's memory load.
+  float f0[4], f1[4], f2[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) nx[i] = load_dt(a, bi, h, 0, 4 * lane + i);
+  for (int i = 0; i < 4; ++i) {
+    f0[i] = load_dt<DT_BF16>(a, bi, h, nci, 0, 4 * lane + i);
+    f1[i] = load_dt<DT_BF16>(a, bi, h, nci, 1, 4 * lane + i);
+    f2[i] = load_dt<DT_BF16>(a, bi, h, nci, 2, 4 * lane + i);
+  }
 #pragma unroll 1
-  for (int c = 0; c < a.nci; ++c) {
-    const int buf = c & 1;
-    const int64_t t0 = (int64_t)c * QI;
-    float d[4], run = 0.f, cs[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      d[i] = (t0 + 4 * lane + i < a.L) ? dt_process(nx[i].raw, bias, a.softplus, a.lo, a.hi) : 0.f;
-      run += d[i] * Ah;
-      cs[i] = run;
-      nx[i] = load_dt(a, bi, h, c + 1, 4 * lane + i);
-    }
-    const float excl = warp_incl_scan(run) - run;
-    // the arrays of chunk c-2 (same buffer) must be released by every reader
-    if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) return;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      m->dA[buf][4 * lane + i] = cs[i] + excl;
-      m->dt[buf][4 * lane + i] = d[i];
-    }
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[DA_READY0 + buf]);
+  for (int c = 0; c < nci; c += 3) {
+    if (!prep_chunk<DT_BF16>(a, m, bi, h, nci, c, Ah, bias, lane, f0)) return;
+    if (c + 1 < nci && !prep_chunk<DT_BF16>(a, m, bi, h, nci, c + 1, Ah, bias, lane, f1)) return;
+    if (c + 2 < nci && !prep_chunk<DT_BF16>(a, m, bi, h, nci, c + 2, Ah, bias, lane, f2)) return;
   }
 }
 
@@ -372,13 +429,23 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   using G_ = Geo<NT>;
   const int yb = c % G_::YB, xb = c % G_::XST;
   const int lane = r & 31;
-  const int64_t pos = (int64_t)c * QI + r;
-  const bool valid = pos < a.L;
+  const Span sp = span_at(a, c);
+  const int64_t pos = (int64_t)sp.t0 + r;
+  const bool valid = r < sp.n;
   const int64_t o0 = (((int64_t)bi * a.L + (valid ? pos : 0)) * a.H + h) * PT;
   float* const out_x = a.out_x;
   const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
-  if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;   // also: MMA2(c) done with S
+  if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 8);
   ptx::tc_fence_after();
+  // the previous chunk's bulk store must have read the staging buffer (long done by now)
+  if (c > 0) {
+    if (r == 0) {
+      ptx::bulk_wait_read();
+      ptx::mbar_arrive(&m->bar[OUT_READ]);
+    }
+    if (!wait_bar(m, OUT_READ, (c - 1) & 1, a.status)) return false;
+  }
   const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
   uint8_t* stage = sm + G_::OFF_S;
 #pragma unroll 1
@@ -430,20 +497,20 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
     ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
   }
-  if (r == 0) TRACE(1, c, 5);
   if (lane == 0) ptx::mbar_arrive(&m->bar[STAGED]);
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 9);
   if (r == 0) {
     // all 128 rows staged: one bulk store per 32-column box
     if (!wait_bar(m, STAGED, c & 1, a.status)) return false;
-    ptx::tma_store_3d(&a.tm_out, stage, h * PT, c * QI, bi);
-    ptx::tma_store_3d(&a.tm_out, stage + QI * 128, h * PT + 32, c * QI, bi);
+    ptx::tma_store_3d(&a.tm_out, stage, h * PT, sp.t0, bi);
+    ptx::tma_store_3d(&a.tm_out, stage + QI * 128, h * PT + 32, sp.t0, bi);
     ptx::bulk_commit();
-    ptx::bulk_wait_read();                     // staging buffer read: score buffer free again
-    ptx::mbar_arrive(&m->bar[OUT_READ]);
+    // A short chunk followed by more tokens (a packed sequence ending) also stored rows of
+    // the next chunk, which that chunk stores again: let this store land first.
+    if (sp.n < QI && sp.t0 + QI < a.L) ptx::bulk_wait_all();
   }
-  const bool ok = wait_bar(m, OUT_READ, c & 1, a.status);
-  if (r == 0) TRACE(1, c, 6);
-  return ok;
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 10);
+  return true;
 }
 
 // One 32-column block of scores for row r: v[i] holds CB[r][t] (t = 32*k32 + i) on entry.
@@ -487,33 +554,37 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
   constexpr bool has_seq = HAS_SEQ;
   using G_ = Geo<NT>;
-  uint8_t* S_sm = sm + G_::OFF_S;
   uint8_t* xs_sm = sm + G_::OFF_XS;
   float sdec_prev = 0.f;
+  const int nci = m->nci;
 #pragma unroll 1
-  for (int c = 0; c < a.nci; ++c) {
+  for (int c = 0; c < nci; ++c) {
     const int buf = c & 1, xb = c % G_::XST;
-    const int64_t t0 = (int64_t)c * QI;
-    if (r == 0) TRACE(half, c, 0);
+    const Span sp = span_at(a, c);
+    const int64_t t0 = sp.t0;
+    const int trole = 2 * half + (q == 3);
+    (void)trole;
+    if (q == 0 || q == 3) TRACE(trole, c, 0);
     if (half == 1 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, c - 1, r, sdec_prev)) return;
-    int seqv = (t0 + r < a.L) ? 0 : -1, prev_seq = 0, end_seq = 0, sl0 = 0, sl1 = 0;
-    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
+    int seqv = (r < sp.n) ? 0 : -1, prev_seq = 0, end_seq = 0, sl0 = 0, sl1 = 0;
+    const int last_valid = sp.n - 1;
     if (has_seq) {
-      seqv = seq_at(a, bi, t0 + r);
+      seqv = (r < sp.n) ? seq_at(a, bi, t0 + r) : -1;
       prev_seq = c == 0 ? 0 : seq_at(a, bi, t0 - 1);
       end_seq = seq_at(a, bi, t0 + last_valid);
       sl0 = seq_at(a, bi, t0 + half * 32 + lane);
       sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
     }
     if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
-    if (r == 0) TRACE(half, c, 1);
     const float dA = m->dA[buf][r];
+    if (q == 0 || q == 3) TRACE(trole, c, 2);
 
     if (half == 0) {
       // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
       const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(m->dA[buf][QI - 1] - dA) * m->dt[buf][r] : 0.f;
       if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
       if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
+      if (q == 0 || q == 3) TRACE(trole, c, 3);
       const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
@@ -525,27 +596,23 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         ptx::mbar_arrive(&m->bar[XS_FULL]);
         ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
       }
-      // the score buffer still holds the previous chunk's staged output until its bulk
-      // store has read it
-      if (c > 0 && !wait_bar(m, OUT_READ, (c - 1) & 1, a.status)) return;
+      if (q == 0 || q == 3) TRACE(trole, c, 4);
     }
 
     // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
-    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 6);
     if (!wait_bar(m, B_CB, c & 1, a.status)) return;
-    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 7);
+    if (q == 0 || q == 3) TRACE(trole, c, 6);
     ptx::tc_fence_after();
     const float dA_R = m->dA[buf][q * 32];
     const float u = __expf(dA - dA_R);
 #pragma unroll 1
     for (int kk = 0; kk < 2; ++kk) {
       const int k32 = half + 2 * kk;
-      uint8_t* Srow = S_sm + (k32 >> 1) * (QI * 128);
-      const int j0 = (k32 & 1) * 4;
+      // bf16 scores of this block replace the first 16 of its 32 CB columns (read first)
+      const uint32_t tS = tmem + COL_CB + k32 * 32;
       if (k32 > q) {
-#pragma unroll
-        for (int sub = 0; sub < 4; ++sub)
-          *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) = make_uint4(0, 0, 0, 0);
+        const uint32_t zero[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+        ptx::tmem_st16(tS, zero);
         continue;
       }
       const int tl = k32 * 32 + lane;
@@ -561,27 +628,25 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       if (fac) score_block<HAS_SEQ, true, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
       else if (diag) score_block<HAS_SEQ, false, true>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
       else score_block<HAS_SEQ, false, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
+      uint32_t pk[16];
 #pragma unroll
-      for (int sub = 0; sub < 4; ++sub)
-        *reinterpret_cast<uint4*>(Srow + ptx::sw128_off(r, j0 + sub)) =
-            make_uint4(pack_bf16(v[8 * sub], v[8 * sub + 1]), pack_bf16(v[8 * sub + 2], v[8 * sub + 3]),
-                       pack_bf16(v[8 * sub + 4], v[8 * sub + 5]), pack_bf16(v[8 * sub + 6], v[8 * sub + 7]));
+      for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+      ptx::tmem_st16(tS, pk);
     }
     // rows continuing the previous chunk's sequence read the passed state (rule A9)
     sdec_prev = (seqv == prev_seq) ? __expf(dA) : 0.f;
+    ptx::tmem_st_wait();
     ptx::tc_fence_before();
-    ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
       ptx::mbar_arrive(&m->bar[CB_FREE]);
       ptx::mbar_arrive(&m->bar[S_FULL]);
       ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     }
-    if ((r == 0 || r == 96) && half == 1) TRACE(r == 0 ? 5 : 6, c, 8);
-    if ((r == 0 || r == 96) && half == 0) TRACE(r == 0 ? 0 : 1, c, 8);
+    if (q == 0 || q == 3) TRACE(trole, c, 7);
   }
-  if (half == 1 && a.nci > 0) {
-    if (!output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, a.nci - 1, r, sdec_prev)) return;
+  if (half == 1 && nci > 0) {
+    if (!output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, nci - 1, r, sdec_prev)) return;
     if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
   }
 }
@@ -621,24 +686,28 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
 
   int prev_end = 0;
+  const int nci = m->nci;
 #pragma unroll 1
-  for (int c = 0; c < a.nci; ++c) {
+  for (int c = 0; c < nci; ++c) {
     const int buf = c & 1;
-    const bool more = c + 1 < a.nci;
+    const bool more = c + 1 < nci;
     // chunk decay: 0 when the chunk-end sequence id changes (state_passing_fwd.py:208-225;
     // the id before the first chunk counts as 0)
-    const int64_t t0 = (int64_t)c * QI;
-    const int last_valid = (int)min((int64_t)QI - 1, (int64_t)a.L - 1 - t0);
-    const int end_seq = a.seq_idx ? seq_at(a, bi, t0 + last_valid) : 0;
+    const Span sp = span_at(a, c);
+    const int end_seq = a.seq_idx ? seq_at(a, bi, (int64_t)sp.t0 + sp.n - 1) : 0;
+    // this chunk ends packed sequence sp.vslot: its state after the chunk is that
+    // sequence's final state (chunk_state_fwd.py:448-597 computes the same per sequence)
+    float* const vdst = sp.vslot >= 0 ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
+    TRACE(5, c, 0);
     if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
     const float dA_last = m->dA[buf][QI - 1];
+    TRACE(5, c, 3);
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     const float decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
     prev_end = end_seq;
-    TRACE(2, c, 0);
     if (!wait_bar(m, B_L, c & 1, a.status)) return;   // L_c ready, MMA3(c) done with S_c
-    TRACE(2, c, 1);
+    TRACE(5, c, 1);
     ptx::tc_fence_after();
 #pragma unroll 1
     for (int seg = 0; seg < 2 * G_::NH; ++seg) {
@@ -650,6 +719,10 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       ptx::tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 32; ++i) sv[i] = decay * sv[i] + lv[i];
+      if (vdst != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) vdst[(32 * half + i) * NT + n] = sv[i];
+      }
       if (more) {
         ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
 #pragma unroll
@@ -670,7 +743,7 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       ptx::mbar_arrive(&m->bar[L_FREE]);
       if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
     }
-    TRACE(2, c, 2);
+    TRACE(5, c, 2);
   }
 }
 
@@ -720,6 +793,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[OUT_READ], 1);
     ptx::mbar_init(&m->bar[DRAIN], 1);
     m->abort = 0;
+    m->nci = a.sched_n ? *a.sched_n : a.nci;
     ptx::fence_mbar_init();
   }
   if (threadIdx.x < PT)
@@ -743,7 +817,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   } else if (warp == 1) {
     if (lane == 0) mma_issuer<NT>(a, sm, m);
   } else if (warp == 2) {
-    prep_worker(a, m, bi, h);
+    if (a.dt_bf16) prep_worker<true>(a, m, bi, h);
+    else prep_worker<false>(a, m, bi, h);
   } else if (warp == 3) {
     // spare warp
   } else if (warp < 12) {
@@ -756,6 +831,110 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(m->tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chunk schedule for varlen states (one block of 1024 threads).  Segment j of the packed
+// row is [p_j, p_{j+1}) with p_0 = 0, p_{k+1} = cu[k] (k = 0..S, clamped to [0, L] and made
+// non-decreasing) and p_{S+2} = L; segment k+1 is packed sequence k.  Each segment is cut
+// into 128-token chunks from its own start; the last chunk of sequence k carries slot k.
+// Empty sequences get a zero state (as chunk_state_fwd.py's varlen path yields for them).
+// Writes the chunk count to hdr[0] and at most `cap` entries plus the {L, -1} sentinel.
+// ---------------------------------------------------------------------------
+constexpr int SCHED_THREADS = 1024;
+
+__global__ void __launch_bounds__(SCHED_THREADS) tc_schedule_kernel(const int32_t* __restrict__ cu, int S, int L,
+                                                                    int cap, int* __restrict__ hdr,
+                                                                    int2* __restrict__ sched, float* vstates,
+                                                                    int64_t vstride) {
+  __shared__ int wred[32];
+  __shared__ int carry_max, carry_cnt, nempty;
+  __shared__ int empty_list[SCHED_THREADS];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const unsigned full = 0xffffffffu;
+  if (tid == 0) {
+    carry_max = 0;
+    carry_cnt = 0;
+  }
+  const int nseg = S + 2;
+  for (int base = 0; base < nseg; base += SCHED_THREADS) {
+    if (tid == 0) nempty = 0;
+    __syncthreads();
+    const int j = base + tid;
+    const int cmax = carry_max, ccnt = carry_cnt;
+    int e = 0;
+    if (j <= S) e = min(max(cu[j], 0), L);
+    else if (j == S + 1) e = L;
+    // inclusive max-scan of the segment ends -> non-decreasing ends
+    int v = e;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(full, v, o);
+      if (lane >= o) v = max(v, t);
+    }
+    if (lane == 31) wred[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      int t = wred[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(full, t, o);
+        if (lane >= o) t = max(t, u);
+      }
+      wred[lane] = t;
+    }
+    __syncthreads();
+    const int before = max(cmax, w > 0 ? wred[w - 1] : 0);   // end of the segment before this warp
+    const int pend = max(v, before);
+    int pstart = __shfl_up_sync(full, pend, 1);
+    if (lane == 0) pstart = before;
+    const int tile_max = max(cmax, wred[31]);
+    __syncthreads();
+    const int len = j < nseg ? pend - pstart : 0;
+    const int nch = (len + QI - 1) / QI;
+    // exclusive sum-scan of the chunk counts
+    int c = nch;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(full, c, o);
+      if (lane >= o) c += t;
+    }
+    if (lane == 31) wred[w] = c;
+    __syncthreads();
+    if (w == 0) {
+      int t = wred[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(full, t, o);
+        if (lane >= o) t += u;
+      }
+      wred[lane] = t;
+    }
+    __syncthreads();
+    const int off = ccnt + (w > 0 ? wred[w - 1] : 0) + c - nch;
+    const bool is_seq = j >= 1 && j <= S;
+    for (int i = 0; i < nch; ++i)
+      if (off + i < cap) sched[off + i] = make_int2(pstart + QI * i, (is_seq && i == nch - 1) ? j - 1 : -1);
+    if (is_seq && len == 0) empty_list[atomicAdd(&nempty, 1)] = j - 1;
+    const int tile_cnt = wred[31];
+    __syncthreads();
+    if (tid == 0) {
+      carry_max = tile_max;
+      carry_cnt = ccnt + tile_cnt;
+    }
+    const int ne = nempty;
+    if (vstates != nullptr)
+      for (int k = 0; k < ne; ++k) {
+        float* dst = vstates + (int64_t)empty_list[k] * vstride;
+        for (int64_t i = tid; i < vstride; i += SCHED_THREADS) dst[i] = 0.f;
+      }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const int n = min(carry_cnt, cap);
+    hdr[0] = n;
+    sched[n] = make_int2(L, -1);
   }
 }
 
@@ -798,7 +977,15 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint6
 
 bool tc_supported(const ssd_fwd_params_t* p) {
   if (p->dtype != SSD_DTYPE_BF16 || p->headdim != PT || (p->dstate != 128 && p->dstate != 256)) return false;
-  if (p->dA_cumsum || p->dt_out || p->varlen_states) return false;
+  if (p->dA_cumsum || p->dt_out) return false;
+  // varlen states come from the per-sequence chunk schedule, which needs the seq_idx masks
+  // inside the chunks it still shares with other sequences' rows.  With initial states the
+  // reference's varlen result depends on its chunking (the first sequence sees the initial
+  // state only if it crosses a chunk boundary, chunk_state_fwd.py:448-597), so those
+  // calls stay on the stage pipeline, which follows it exactly.
+  if (p->varlen_states &&
+      (!p->seq_idx || !p->cu_seqlens || p->num_seqs <= 0 || p->batch != 1 || p->initial_states))
+    return false;
   if (p->batch * p->nheads > 0x7fffffff) return false;
   const uintptr_t al = 15;
   if ((reinterpret_cast<uintptr_t>(p->x) | reinterpret_cast<uintptr_t>(p->B) | reinterpret_cast<uintptr_t>(p->C) |
@@ -820,12 +1007,18 @@ bool trace_enabled() {
   return on == 1;
 }
 
-// 256 bytes: device status word; with SSD_TC_TRACE=1 a 64 KB phase trace follows (debug).
-size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
-  return tc_supported(p) ? 256 + (trace_enabled() ? 8 * 64 * 16 * 8 : 0) : 0;
+// Workspace: 256 bytes of device status word; with varlen states the chunk schedule
+// (an 8-byte header, then cap + 1 int2 entries); with SSD_TC_TRACE=1 a 64 KB phase trace.
+int64_t sched_cap(const ssd_fwd_params_t* p) { return (p->seqlen + QI - 1) / QI + p->num_seqs + 2; }
+size_t sched_bytes(const ssd_fwd_params_t* p) {
+  return p->varlen_states ? (size_t)(8 + 8 * (sched_cap(p) + 1) + 255) / 256 * 256 : 0;
 }
 
-int tc_num_launches(const ssd_fwd_params_t*) { return 1; }
+size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
+  return tc_supported(p) ? 256 + sched_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 : 0) : 0;
+}
+
+int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 2 : 1; }
 
 int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st) {
   TcArgs a;
@@ -843,8 +1036,9 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.dt = p->dt; a.A = p->A; a.dt_bias = p->dt_bias; a.D = p->D;
   a.x = (const bf16*)p->x; a.z = (const bf16*)p->z; a.init = p->initial_states; a.seq_idx = p->seq_idx;
   a.out = p->out; a.out_x = p->z ? p->out_x : nullptr; a.final_states = p->final_states;
+  a.varlen_states = p->varlen_states;
   a.status = (unsigned*)workspace;
-  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256) : nullptr;
+  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256 + sched_bytes(p)) : nullptr;
   typedef void (*KernelFn)(TcArgs);
   static const KernelFn kernels[8] = {
       ssd_fused_tc_kernel<128, false, false>, ssd_fused_tc_kernel<128, false, true>,
@@ -864,6 +1058,19 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) {
     set_last_error("cudaMemsetAsync of the status word failed");
     return SSD_ERR_CUDA;
+  }
+  if (p->varlen_states) {
+    const int64_t cap = sched_cap(p);
+    if (cap > 0x3fffffff) {
+      set_last_error("varlen chunk schedule too long");
+      return SSD_ERR_UNSUPPORTED;
+    }
+    int* hdr = (int*)((char*)workspace + 256);
+    int2* sched = (int2*)((char*)workspace + 264);
+    tc_schedule_kernel<<<1, SCHED_THREADS, 0, st>>>(p->cu_seqlens, p->num_seqs, (int)L, (int)cap, hdr, sched,
+                                                    p->varlen_states, H * PT * p->dstate);
+    a.sched_n = hdr;
+    a.sched = sched;
   }
   kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
   const cudaError_t e = cudaGetLastError();

@@ -357,3 +357,45 @@ def test_tensor_core_path_state_dims_and_seq_idx(N, lens, z):
                                         seq_idx=seq, dt_softplus=True, return_final_states=True)
     assert rel_l2(out, ref_out) <= TOL["bf16"]
     assert rel_l2(r.final, ref_final) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("N,lens", [(128, [128, 1, 0, 300, 255, 44]), (256, [700, 3, 129, 127, 1]),
+                                    (128, [256, 128, 384])],
+                         ids=["n128-ragged", "n256-long", "n128-aligned"])
+@pytest.mark.parametrize("z", [False, True])
+def test_tensor_core_path_varlen_states(N, lens, z):
+    """Varlen final states on the fused kernel: every packed sequence is tiled from its own
+    start, so its state is read off the running state at its last chunk.  Covers an empty
+    sequence, a one-token sequence, sequence ends on and off 128-token boundaries and a
+    ragged last chunk; the outputs of rows stored twice (a short chunk's tail) must match."""
+    from mamba2_b200.runner import SsdForward
+    L = sum(lens)
+    cfg = S.SsdConfig("t", 1, L, 8, 64, 2, N, 128, "bf16", has_z=z, return_final=True)
+    inp = S.make_ssd_inputs(cfg, 7 + N + len(lens))
+    seq = np.repeat(np.arange(len(lens)), lens)[None].astype(np.int32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    d = dev_inputs(inp, "bf16")
+    r = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 128, D=d["D"], z=d["z"], dt_bias=d["dt_bias"],
+                   seq_idx=to_dev(seq, int32=True), cu_seqlens=to_dev(cu, int32=True), dt_softplus=True,
+                   return_final_states=True)
+    assert r.uses_tc and r.launches_per_step == 2
+    r.varlen.fill_(float("nan"))
+    out = r()
+    torch.cuda.synchronize()
+    assert int(r.workspace[:4].view(torch.int32).item()) == 0
+    ref_out, ref_final, ref_var = R.ssd_combined(
+        inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], 128, D=inp["D"], z=inp["z"], dt_bias=inp["dt_bias"],
+        seq_idx=seq, cu_seqlens=cu, dt_softplus=True, return_final_states=True, return_varlen_states=True)
+    assert rel_l2(out, ref_out) <= TOL["bf16"]
+    assert rel_l2(r.final, ref_final) <= TOL["bf16"]
+    assert torch.isfinite(r.varlen).all()
+    for k in range(len(lens)):
+        if lens[k] == 0:
+            assert (r.varlen[k] == 0).all()
+        else:
+            assert rel_l2(r.varlen[k], ref_var[k]) <= TOL["bf16"], k
+    # deterministic: a second call writes the same bytes
+    out1 = out.clone()
+    r()
+    torch.cuda.synchronize()
+    assert torch.equal(out, out1)
