@@ -16,15 +16,20 @@
 //   MMA_L Lt[n][p]  = B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM
 //   E3    S_{c+1}   = keep_c exp(dA_last_c) S_c + Lt    (TMEM f32)  -> bf16 smem for MMA3
 //   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi + D x ; * silu(z)
-// Decay factors are always formed from differences of the in-chunk cumulative sums
-// (never exp(dA_m) * exp(-dA_t)), as ssd_naive.py:264-268 does.
+// Decay factors come from differences of the in-chunk cumulative sums, as in
+// ssd_naive.py:264-268, never from exp(dA_m) * exp(-dA_t) over a whole chunk.  Within one
+// 32-token column block k they factor as exp(dA_m - dA_{32k}) * exp(dA_{32k} - dA_t) when
+// dA is non-increasing and the block's range is at most 60 (both factors then stay in
+// float range); other blocks are formed element by element.
 //
 // The only serial dependence between chunks is the state: E3(c) -> MMA3(c+1) -> E3(c+1).
 // Everything else is pipelined around it by warp role (16 warps, so every SM sub-partition
 // holds 4 warps and each thread may use 128 registers):
 //   warp 0      TMA producer (lane 0)
-//   warp 1      MMA issuer (lane 0); owns the TMEM allocation (all 512 columns)
-//   warp 2      prep: processed dt and cumulative dA of each chunk (shared arrays); warp 3 spare
+//   warp 1      MMA issuer A (lane 0): MMA1, MMA2; owns the TMEM allocation (512 columns)
+//   warp 2      dA producer (lane 0): the chunk's cumulative dA and decay factors, computed
+//               by the dt pre-pass, bulk-copied into shared memory
+//   warp 3      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
 //   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
 //   warps 8-11  SB: output epilogue E4 of the previous chunk (staged in shared memory and
 //               written by a TMA bulk store), then score column blocks 1 and 3
@@ -87,14 +92,16 @@ enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0,
            DA_FREE1, L_FREE, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA commit, SA warps (xs), SB warps (D x)
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4;   // MMA2 commit, SA warps (xs and D x)
 constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
-  uint64_t bar[NBARS];
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
-  float dt[2][QI];      // processed dt
+  // Per token t of 32-token block k: w_t = exp(dA_{32k} - dA_t) dt_t when block k is
+  // factored (block_factored), else the processed dt_t.
+  float dt[2][QI];
   float Dv[PT];         // skip coefficient per head-dim column (0 without D)
+  uint64_t bar[NBARS];
   uint32_t tmem_base;
   int nci;              // chunks of this CTA's walk (from the schedule when there is one)
   volatile int abort;
@@ -118,6 +125,8 @@ struct TcArgs {
   float* out_x;
   float* final_states;
   float* varlen_states;        // (num_seqs, H, P, N) or null
+  const float* dtprep;         // per (b, h, chunk): dA[128] then w[128], from tc_dt_prep_kernel
+  int prep_cap;                // chunk slots per (b, h) in dtprep
   const int* sched_n;          // chunk count written by the schedule kernel, or null
   const int2* sched;           // {t0, varlen slot or -1} per chunk, entry nci = {L, -1}
   unsigned* status;
@@ -144,9 +153,10 @@ struct TcArgs {
 constexpr long long TIMEOUT_CYCLES = 4000000000LL;
 
 // Bounded wait.  Returns false (after flagging the CTA and the status word) on timeout or
-// when another role of this CTA already gave up.
-__device__ __forceinline__ bool wait_bar(Misc* m, int id, uint32_t parity, unsigned* status) {
-  if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
+// when another role of this CTA already gave up.  One probe is inlined; the spin loop is
+// a single out-of-line copy, so the many wait sites add little to the hot code (which
+// otherwise outgrows the instruction cache).
+__device__ __noinline__ bool wait_bar_slow(Misc* m, int id, uint32_t parity, unsigned* status) {
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
@@ -160,6 +170,11 @@ __device__ __forceinline__ bool wait_bar(Misc* m, int id, uint32_t parity, unsig
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool wait_bar(Misc* m, int id, uint32_t parity, unsigned* status) {
+  if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
+  return wait_bar_slow(m, id, parity, status);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -236,22 +251,50 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
 }
 
 // ---------------------------------------------------------------------------
-// MMA issuer (warp 1, lane 0)
+// dA producer (warp 2, lane 0): each chunk's dA and w arrays (from the dt pre-pass) into the
+// shared arrays of its parity, as soon as the readers of chunk c-2 have released them.
+// Kept apart from the C/B/x producer so neither waits on the other's consumers.
+// ---------------------------------------------------------------------------
+__device__ void da_producer(const TcArgs& a, Misc* m, int bi, int h) {
+  const int nci = m->nci;
+  int c = 0;
+  for (; c < nci; ++c) {
+    const int buf = c & 1;
+    if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) break;
+    const float* src = a.dtprep + (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
+    ptx::mbar_arrive_expect_tx(&m->bar[DA_READY0 + buf], 2 * QI * 4);
+    ptx::bulk_load(m->dA[buf], src, QI * 4, &m->bar[DA_READY0 + buf]);
+    ptx::bulk_load(m->dt[buf], src + QI, QI * 4, &m->bar[DA_READY0 + buf]);
+  }
+  // drain: never leave the CTA with bulk copies still landing in its shared memory
+  const long long t0 = clock64();
+  for (int cc = (c >= 2 ? c - 2 : 0); cc < c; ++cc)
+    while (!ptx::mbar_try_wait(&m->bar[DA_READY0 + (cc & 1)], (cc >> 1) & 1) && clock64() - t0 < TIMEOUT_CYCLES) {
+    }
+}
+
+// ---------------------------------------------------------------------------
+// MMA issuers.  The four MMAs of a chunk have different inputs, and a single issuer in a
+// fixed order would queue the state chain (MMA3, MMA_L) behind MMA1, which waits for the
+// score warps.  So two threads issue, each in chunk order with blocking waits:
+//   A (warp 1, lane 0)  MMA1(c)  CB = C.B^T   after C,B(c) loaded and E2(c-1) done with CB
+//                       MMA2(c)  Y += S.x     after the scores (in TMEM), x(c), Y buffer free
+//   B (warp 3, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, Yi buffer free
+//                       MMA_L(c) L = B^T.xs   after xs(c) and T done with L(c-1)
+// MMA2(c) and MMA1(c+1) share the TMEM columns of the scores; both come from thread A,
+// whose tcgen05.mma execute in issue order.  The C/B ring stage and B_Y each take one
+// commit from both threads; B_CB and X_EMPTY come from A, B_L from B.
 // ---------------------------------------------------------------------------
 template <int NT>
-__device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
+__device__ void mma_issuer_a(const TcArgs& a, uint8_t* sm, Misc* m) {
   using G_ = Geo<NT>;
   const uint32_t tmem = m->tmem_base;
   const uint32_t base = ptx::smem_u32(sm);
   constexpr uint32_t ID_CB = ptx::idesc_bf16_f32(128, 128, 0, 0);
-  constexpr uint32_t ID_YI = ptx::idesc_bf16_f32(128, 64, 0, 1);
-  constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
   constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
   const int nci = m->nci;
   for (int c = 0; c < nci; ++c) {
     const int yb = c % G_::YB, xb = c % G_::XST;
-    TRACE(4, c, 0);
-    const uint32_t colY = COL_Y0 + 128 * yb, colYI = COL_YI0 + 128 * yb;
     // MMA1: CB = C . B^T, summed over the 128-column halves of the state dim (K-major)
     for (int hh = 0; hh < G_::NH; ++hh) {
       const int k = c * G_::NH + hh;
@@ -267,10 +310,49 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
       }
     }
     ptx::mma_commit(&m->bar[B_CB]);
+    for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
     TRACE(4, c, 1);
+    // MMA2: Y (+)= S . x  (A = bf16 scores in TMEM: tokens 32k..32k+31 in the first 16
+    // columns of CB block k; B = x [t][p] MN-major).  With D, Y already holds D x.
+    if (!wait_bar(m, S_FULL, c & 1, a.status)) goto drain;
+    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
+    if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
+    ptx::tc_fence_after();
+    {
+      const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
+#pragma unroll
+      for (int i = 0; i < QI / 16; ++i)
+        ptx::mma_f16_ts(tmem + COL_Y0 + 128 * yb, tmem + COL_CB + 32 * (i >> 1) + 8 * (i & 1),
+                        ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, (i > 0 || a.D_ndim != 0) ? 1u : 0u);
+    }
+    ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
+    ptx::mma_commit(&m->bar[B_Y0 + yb]);
+    TRACE(4, c, 5);
+  }
+drain:
+  // wait (bounded) until every MMA this thread issued has completed
+  ptx::mma_commit(&m->bar[DRAIN]);
+  const long long t0 = clock64();
+  while (!ptx::mbar_try_wait(&m->bar[DRAIN], 0) && clock64() - t0 < TIMEOUT_CYCLES) {
+  }
+}
+
+template <int NT>
+__device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
+  using G_ = Geo<NT>;
+  const uint32_t tmem = m->tmem_base;
+  const uint32_t base = ptx::smem_u32(sm);
+  constexpr uint32_t ID_YI = ptx::idesc_bf16_f32(128, 64, 0, 1);
+  constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
+  const int nci = m->nci;
+  for (int c = 0; c < nci; ++c) {
+    const int yb = c % G_::YB;
+    for (int hh = 0; hh < G_::NH; ++hh) {
+      const int k = c * G_::NH + hh;
+      if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) goto drain;
+    }
     // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)  -- the state chain
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
-    TRACE(4, c, 2);
     if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
@@ -278,15 +360,15 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t offa = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
-        ptx::mma_f16(tmem + colYI, ptx::sdesc_sw128(sC + offa, 16, 1024),
+        ptx::mma_f16(tmem + COL_YI0 + 128 * yb, ptx::sdesc_sw128(sC + offa, 16, 1024),
                      ptx::sdesc_sw128(base + G_::OFF_ST + hh * (128 * 128) + i * 2048, 8192, 1024), ID_YI,
                      (hh > 0 || i > 0) ? 1u : 0u);
       }
     }
+    TRACE(4, c, 2);
     // MMA_L: L_c = B^T . xs, one 128-row half of the state dim per ring stage
     if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
     if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) goto drain;
-    TRACE(4, c, 3);
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
       const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
@@ -295,29 +377,12 @@ __device__ void mma_issuer(const TcArgs& a, uint8_t* sm, Misc* m) {
         ptx::mma_f16(tmem + G_::COL_L + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
                      ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
     }
-    for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
     ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
-    // MMA2: Y = S . x   (A = bf16 scores in TMEM, B = x [t][p] MN-major).  The scores of
-    // tokens 32k..32k+31 sit in the first 16 columns of CB block k; MMA1(c+1), issued after
-    // this by the same thread, overwrites them only after these reads (tcgen05.mma of one
-    // thread execute in issue order).
-    if (!wait_bar(m, S_FULL, c & 1, a.status)) goto drain;
-    TRACE(4, c, 4);
-    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
-    ptx::tc_fence_after();
-    {
-      const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
-#pragma unroll
-      for (int i = 0; i < QI / 16; ++i)
-        ptx::mma_f16_ts(tmem + colY, tmem + COL_CB + 32 * (i >> 1) + 8 * (i & 1),
-                        ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0);
-    }
+    for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
     ptx::mma_commit(&m->bar[B_Y0 + yb]);
-    ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
-    TRACE(4, c, 5);
+    TRACE(4, c, 3);
   }
 drain:
-  // wait (bounded) until every issued MMA has completed
   ptx::mma_commit(&m->bar[DRAIN]);
   const long long t0 = clock64();
   while (!ptx::mbar_try_wait(&m->bar[DRAIN], 0) && clock64() - t0 < TIMEOUT_CYCLES) {
@@ -355,68 +420,58 @@ __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
 }
 
 // ---------------------------------------------------------------------------
-// prep (warp 2): processed dt and in-chunk cumulative dA into the shared arrays
-// (double-buffered by chunk parity).  Lane l owns rows 4l..4l+3; one warp, so no
-// cross-warp barrier is needed.
+// dt pre-pass (its own launch, before the fused kernel): for every (batch, head, chunk) the
+// processed dt (bias, softplus, clamp; chunk_cumsum_fwd.py:221-231), the in-chunk cumulative
+// dA = cumsum(dt * A) and the decay column factors w, 1 KB per chunk.  The fused kernel's
+// producer bulk-copies each chunk's 1 KB into shared memory, so no warp of that kernel
+// waits on these scattered loads (several microseconds each under its memory traffic).
+// Decay factors per 32-token block k: exp(dA_m - dA_t) = exp(dA_m - dA_{32k}) * w_t with
+// w_t = exp(dA_{32k} - dA_t) dt_t.  With dA non-increasing (A <= 0, dt >= 0) the first
+// factor is <= 1 for m >= 32k and w_t <= exp(block range); blocks whose range exceeds 60
+// (or every block when dA may increase) store dt_t and are formed element by element.
 // ---------------------------------------------------------------------------
-// One chunk of prep: consumes f (raw dt of chunk c), then refills f with chunk c + 3.
-template <bool DT_BF16>
-__device__ __forceinline__ bool prep_chunk(const TcArgs& a, Misc* m, int bi, int h, int nci, int c, float Ah,
-                                           float bias, int lane, float (&f)[4]) {
-  const int buf = c & 1;
-  const int n = span_at(a, c).n;
-  TRACE(7, c, 0);
-  float d[4], run = 0.f, cs[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    d[i] = (4 * lane + i < n) ? dt_process(f[i], bias, a.softplus, a.lo, a.hi) : 0.f;
-    run += d[i] * Ah;
-    cs[i] = run;
-  }
-  TRACE(7, c, 4);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[i] = load_dt<DT_BF16>(a, bi, h, nci, c + 3, 4 * lane + i);
-  }
-  const float excl = warp_incl_scan(run) - run;
-  TRACE(7, c, 3);
-  // the arrays of chunk c-2 (same buffer) must be released by every reader
-  if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) return false;
-  TRACE(7, c, 1);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m->dA[buf][4 * lane + i] = cs[i] + excl;
-    m->dt[buf][4 * lane + i] = d[i];
-  }
-  __syncwarp();
-  if (lane == 0) ptx::mbar_arrive(&m->bar[DA_READY0 + buf]);
-  TRACE(7, c, 2);
-  return true;
+constexpr float FAC_RANGE = 60.f;
+
+__device__ __forceinline__ bool block_factored(bool factor, const float* dA, int k) {
+  return factor && (dA[32 * k] - dA[32 * k + 31] <= FAC_RANGE);
 }
 
 template <bool DT_BF16>
-__device__ void prep_worker(const TcArgs& a, Misc* m, int bi, int h) {
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__ TcArgs a, float* __restrict__ out) {
+  const int c = blockIdx.x, bi = blockIdx.y;
+  const int nci = a.sched_n ? *a.sched_n : a.nci;
+  const int h = blockIdx.z * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (c >= nci || h >= a.H) return;
+  const Span sp = span_at(a, c);
   const float Ah = a.A[h];
   const float bias = a.dt_bias ? a.dt_bias[h] : 0.f;
-  const int nci = m->nci;
-  if (nci <= 0) return;
-  // Raw dt (128 separate lines per chunk) is loaded three chunks before its use into one
-  // of three register sets; the loop is unrolled by three so no set is copied (a copy
-  // would wait for its load): these loads take microseconds under the kernel's memory load.
-  float f0[4], f1[4], f2[4];
+  const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
+  float d[4], run = 0.f, cs[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    f0[i] = load_dt<DT_BF16>(a, bi, h, nci, 0, 4 * lane + i);
-    f1[i] = load_dt<DT_BF16>(a, bi, h, nci, 1, 4 * lane + i);
-    f2[i] = load_dt<DT_BF16>(a, bi, h, nci, 2, 4 * lane + i);
+    const int r = 4 * lane + i;
+    float raw = 0.f;
+    if (r < sp.n) {
+      const int64_t di = ((int64_t)bi * a.L + sp.t0 + r) * a.H + h;
+      raw = DT_BF16 ? __bfloat162float(((const bf16*)a.dt)[di]) : ((const float*)a.dt)[di];
+    }
+    d[i] = r < sp.n ? dt_process(raw, bias, a.softplus, a.lo, a.hi) : 0.f;
+    run += d[i] * Ah;
+    cs[i] = run;
   }
-#pragma unroll 1
-  for (int c = 0; c < nci; c += 3) {
-    if (!prep_chunk<DT_BF16>(a, m, bi, h, nci, c, Ah, bias, lane, f0)) return;
-    if (c + 1 < nci && !prep_chunk<DT_BF16>(a, m, bi, h, nci, c + 1, Ah, bias, lane, f1)) return;
-    if (c + 2 < nci && !prep_chunk<DT_BF16>(a, m, bi, h, nci, c + 2, Ah, bias, lane, f2)) return;
-  }
+  const float excl = warp_incl_scan(run) - run;
+  float dAv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dAv[i] = cs[i] + excl;
+  const float dAs = __shfl_sync(0xffffffffu, dAv[0], lane & ~7);
+  const float dAe = __shfl_sync(0xffffffffu, dAv[3], lane | 7);
+  const bool fk = factor && (dAs - dAe <= FAC_RANGE);
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = fk ? __expf(dAs - dAv[i]) * d[i] : d[i];
+  float* o = out + (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
+  reinterpret_cast<float4*>(o)[lane] = make_float4(dAv[0], dAv[1], dAv[2], dAv[3]);
+  reinterpret_cast<float4*>(o + QI)[lane] = make_float4(w[0], w[1], w[2], w[3]);
 }
 
 // Output epilogue of chunk c (run by SB): out = Y + sdec Yi + D x, z gate.  Row r is
@@ -427,14 +482,21 @@ template <int NT, bool HAS_Z>
 __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tmem, int bi, int h, int c, int r,
                              float sdec) {
   using G_ = Geo<NT>;
-  const int yb = c % G_::YB, xb = c % G_::XST;
+  const int yb = c % G_::YB;
   const int lane = r & 31;
   const Span sp = span_at(a, c);
   const int64_t pos = (int64_t)sp.t0 + r;
   const bool valid = r < sp.n;
-  const int64_t o0 = (((int64_t)bi * a.L + (valid ? pos : 0)) * a.H + h) * PT;
+  const int64_t o0 = (((int64_t)bi * a.L + (valid ? pos : sp.t0)) * a.H + h) * PT;
   float* const out_x = a.out_x;
-  const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
+  // z of this row, loaded unconditionally (rows past the chunk read a valid row and are
+  // never stored) and issued before the waits so its latency overlaps them
+  uint4 zq[8];
+  if (HAS_Z) {
+    const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) zq[k] = __ldg(zp + k);
+  }
   if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 8);
   ptx::tc_fence_after();
@@ -446,31 +508,23 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     }
     if (!wait_bar(m, OUT_READ, (c - 1) & 1, a.status)) return false;
   }
-  const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
   uint8_t* stage = sm + G_::OFF_S;
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float y[32], yi[32];
     ptx::tmem_ld32(tmem + COL_Y0 + 128 * yb + 32 * half, y);
     ptx::tmem_ld32(tmem + COL_YI0 + 128 * yb + 32 * half, yi);
-    uint32_t xw[16], zw[16];
+    uint32_t zw[16];
+    if (HAS_Z) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint4 xq = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * half + k));
-      xw[4 * k] = xq.x; xw[4 * k + 1] = xq.y; xw[4 * k + 2] = xq.z; xw[4 * k + 3] = xq.w;
-      if (HAS_Z) {
-        const uint4 zq = valid ? __ldg(zp + 4 * half + k) : make_uint4(0, 0, 0, 0);
-        zw[4 * k] = zq.x; zw[4 * k + 1] = zq.y; zw[4 * k + 2] = zq.z; zw[4 * k + 3] = zq.w;
+      for (int k = 0; k < 4; ++k) {
+        const uint4 w = half == 0 ? zq[k] : zq[4 + k];
+        zw[4 * k] = w.x; zw[4 * k + 1] = w.y; zw[4 * k + 2] = w.z; zw[4 * k + 3] = w.w;
       }
     }
-    const float* Dv = m->Dv + 32 * half;
     ptx::tmem_ld_wait();
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const float2 f = unpack_bf16(xw[k]);
-      y[2 * k] = fmaf(sdec, yi[2 * k], y[2 * k]) + Dv[2 * k] * f.x;
-      y[2 * k + 1] = fmaf(sdec, yi[2 * k + 1], y[2 * k + 1]) + Dv[2 * k + 1] * f.y;
-    }
+    for (int k = 0; k < 32; ++k) y[k] = fmaf(sdec, yi[k], y[k]);   // Y already holds D x
     if (HAS_Z) {
       if (out_x != nullptr && valid) {
 #pragma unroll
@@ -495,9 +549,8 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   __syncwarp();
   if (lane == 0) {
     ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
-    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+    ptx::mbar_arrive(&m->bar[STAGED]);
   }
-  if (lane == 0) ptx::mbar_arrive(&m->bar[STAGED]);
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 9);
   if (r == 0) {
     // all 128 rows staged: one bulk store per 32-column box
@@ -516,23 +569,52 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
 // One 32-column block of scores for row r: v[i] holds CB[r][t] (t = 32*k32 + i) on entry.
 // FAC: t is below the quadrant's diagonal block, the decay is u_r * vl_t (vl in lane i);
 // otherwise exp(dA_r - dA_t) dt_t per element, masked to t <= r on the diagonal block.
-template <bool HAS_SEQ, bool FAC, bool DIAG>
-__device__ __forceinline__ void score_block(float (&v)[32], float u, float vl, float dA, const float* dAc,
-                                            const float* dtc, int sl, int seqv, int lane) {
+// One 32-column block of scores for row r (v holds CB[r][t], t = block start + i, on
+// entry; packed bf16 pairs on exit).  Factored blocks: decay u_r * w_t, w read from shared
+// memory (the same address in every lane).  Columns i > lim are masked (lim = lane on the
+// diagonal block, 31 below it).
+template <bool HAS_SEQ>
+__device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (&pk)[16], float u, const float* wc,
+                                                int lim, int sl, int seqv) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    bool ok = !DIAG || i <= lane;
-    if (HAS_SEQ) {
-      // every lane takes part in the shuffle (a short-circuited __shfl_sync would diverge)
-      const int st = __shfl_sync(0xffffffffu, sl, i);
-      ok = ok && (st == seqv);
+  for (int i4 = 0; i4 < 8; ++i4) {
+    const float4 w4 = *reinterpret_cast<const float4*>(wc + 4 * i4);
+    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = 4 * i4 + j;
+      bool ok = i <= lim;
+      if (HAS_SEQ) {
+        // every lane takes part in the shuffle (a short-circuited __shfl_sync would diverge)
+        const int st = __shfl_sync(0xffffffffu, sl, i);
+        ok = ok && (st == seqv);
+      }
+      o[j] = ok ? v[i] * (u * wv[j]) : 0.f;
     }
-    if (FAC) {
-      const float w = u * __shfl_sync(0xffffffffu, vl, i);
-      v[i] = ok ? v[i] * w : 0.f;
-    } else {
-      v[i] = v[i] * __expf(ok ? dA - dAc[i] : -INFINITY) * dtc[i];
+    pk[2 * i4] = pack_bf16(o[0], o[1]);
+    pk[2 * i4 + 1] = pack_bf16(o[2], o[3]);
+  }
+}
+
+// Blocks that do not factor (dA may increase, or its range in the block exceeds 60, as for
+// heads with large |A| dt): exp(dA_r - dA_t) dt_t per element.
+template <bool HAS_SEQ>
+__device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
+                                                  const float* dtc, int lim, int sl, int seqv) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float o[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      bool ok = i + j <= lim;
+      if (HAS_SEQ) {
+        const int st = __shfl_sync(0xffffffffu, sl, i + j);   // all lanes shuffle, then combine
+        ok = ok && (st == seqv);
+      }
+      o[j] = v[i + j] * __expf(ok ? dA - dAc[i + j] : -INFINITY) * dtc[i + j];
     }
+    pk[i / 2] = pack_bf16(o[0], o[1]);
   }
 }
 
@@ -547,16 +629,12 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
-  const float Ah = a.A[h];
-  // Below the diagonal block the decay factors as exp(dA_r - dA_R) * exp(dA_R - dA_t)
-  // (R = first row of the quadrant) with both exponents <= 0 when the cumulative sum is
-  // non-increasing (A <= 0, dt >= 0); otherwise every element is formed directly.
-  const bool factor = (Ah <= 0.f) && (a.lo >= 0.f);
   constexpr bool has_seq = HAS_SEQ;
+  const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
   using G_ = Geo<NT>;
   uint8_t* xs_sm = sm + G_::OFF_XS;
-  float sdec_prev = 0.f;
   const int nci = m->nci;
+  float sdec_prev = 0.f;
 #pragma unroll 1
   for (int c = 0; c < nci; ++c) {
     const int buf = c & 1, xb = c % G_::XST;
@@ -581,7 +659,10 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
 
     if (half == 0) {
       // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
-      const float scale = (end_seq >= 0 && seqv == end_seq) ? __expf(m->dA[buf][QI - 1] - dA) * m->dt[buf][r] : 0.f;
+      // exp(dA_last - dA_r) dt_r, from w_r = exp(dA_{32q} - dA_r) dt_r in a factored block
+      const bool fq = block_factored(factor, m->dA[buf], q);
+      const float e1 = __expf(m->dA[buf][QI - 1] - (fq ? m->dA[buf][32 * q] : dA)) * m->dt[buf][r];
+      const float scale = (end_seq >= 0 && seqv == end_seq) ? e1 : 0.f;
       if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
       if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
       if (q == 0 || q == 3) TRACE(trole, c, 3);
@@ -592,10 +673,33 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
             scale_row16(*reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, k)), scale);
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        ptx::mbar_arrive(&m->bar[XS_FULL]);
-        ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+      if (lane == 0) ptx::mbar_arrive(&m->bar[XS_FULL]);
+      if (q == 0 || q == 3) TRACE(trole, c, 8);
+      if (a.D_ndim != 0) {
+        // the skip term starts the Y accumulator: Y(c) = D x in f32, MMA2(c) adds S x
+        const int yb = c % G_::YB;
+        if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return;
+        if (q == 0 || q == 3) TRACE(trole, c, 9);
+#pragma unroll 1
+        for (int hx = 0; hx < 2; ++hx) {
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack_bf16(wv[j]);
+              v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
+              v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
+            }
+          }
+          ptx::tmem_st32(tmem + COL_Y0 + 128 * yb + 32 * hx, v);
+        }
+        ptx::tmem_st_wait();   // ordered before MMA2(c) by the S_FULL arrival below
       }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
       if (q == 0 || q == 3) TRACE(trole, c, 4);
     }
 
@@ -603,8 +707,6 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     if (!wait_bar(m, B_CB, c & 1, a.status)) return;
     if (q == 0 || q == 3) TRACE(trole, c, 6);
     ptx::tc_fence_after();
-    const float dA_R = m->dA[buf][q * 32];
-    const float u = __expf(dA - dA_R);
 #pragma unroll 1
     for (int kk = 0; kk < 2; ++kk) {
       const int k32 = half + 2 * kk;
@@ -615,23 +717,20 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         ptx::tmem_st16(tS, zero);
         continue;
       }
-      const int tl = k32 * 32 + lane;
       const int sl = kk == 0 ? sl0 : sl1;
-      const bool fac = factor && k32 < q;
-      const bool diag = k32 == q;
-      const float vl = fac ? __expf(dA_R - m->dA[buf][tl]) * m->dt[buf][tl] : 0.f;
+      const bool fac = block_factored(factor, m->dA[buf], k32);
+      const int lim = k32 == q ? lane : 31;
       const float* dAc = m->dA[buf] + k32 * 32;
-      const float* dtc = m->dt[buf] + k32 * 32;
+      const float* wc = m->dt[buf] + k32 * 32;
       float v[32];
+      uint32_t pk[16];
       ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);   // one TMEM round trip per block
       ptx::tmem_ld_wait();
-      if (fac) score_block<HAS_SEQ, true, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
-      else if (diag) score_block<HAS_SEQ, false, true>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
-      else score_block<HAS_SEQ, false, false>(v, u, vl, dA, dAc, dtc, sl, seqv, lane);
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+      if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
+      if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv);
+      else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv);
       ptx::tmem_st16(tS, pk);
+      if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
     }
     // rows continuing the previous chunk's sequence read the passed state (rule A9)
     sdec_prev = (seqv == prev_seq) ? __expf(dA) : 0.f;
@@ -768,8 +867,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   if (threadIdx.x == 0) {
     ptx::mbar_init(&m->bar[CB_FULL0], 1);
     ptx::mbar_init(&m->bar[CB_FULL1], 1);
-    ptx::mbar_init(&m->bar[CB_EMPTY0], 1);
-    ptx::mbar_init(&m->bar[CB_EMPTY1], 1);
+    ptx::mbar_init(&m->bar[CB_EMPTY0], 2);   // one commit from each MMA issuer
+    ptx::mbar_init(&m->bar[CB_EMPTY1], 2);
     ptx::mbar_init(&m->bar[X_FULL0], 1);
     ptx::mbar_init(&m->bar[X_FULL1], 1);
     ptx::mbar_init(&m->bar[X_EMPTY0], X_EMPTY_COUNT);
@@ -780,8 +879,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[S_FULL], 8);
     ptx::mbar_init(&m->bar[ST_READY], 4);
     ptx::mbar_init(&m->bar[B_L], 1);
-    ptx::mbar_init(&m->bar[B_Y0], 1);
-    ptx::mbar_init(&m->bar[B_Y1], 1);
+    ptx::mbar_init(&m->bar[B_Y0], 2);
+    ptx::mbar_init(&m->bar[B_Y1], 2);
     ptx::mbar_init(&m->bar[Y_FREE0], 4);
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
     ptx::mbar_init(&m->bar[DA_READY0], 1);
@@ -791,11 +890,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[L_FREE], 4);
     ptx::mbar_init(&m->bar[STAGED], 4);
     ptx::mbar_init(&m->bar[OUT_READ], 1);
-    ptx::mbar_init(&m->bar[DRAIN], 1);
+    ptx::mbar_init(&m->bar[DRAIN], 2);
     m->abort = 0;
     m->nci = a.sched_n ? *a.sched_n : a.nci;
     ptx::fence_mbar_init();
   }
+#ifdef SSD_TC_DEBUG_TRACE
+  if (a.trace && threadIdx.x == 0 && blockIdx.x < 2048) {
+    a.trace[8 * 64 * 16 + 3 * blockIdx.x] = ptx::globaltimer();
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    a.trace[8 * 64 * 16 + 3 * blockIdx.x + 2] = smid;
+  }
+#endif
   if (threadIdx.x < PT)
     m->Dv[threadIdx.x] = a.D_ndim == 1 ? a.D[h] : a.D_ndim == 2 ? a.D[(int64_t)h * PT + threadIdx.x] : 0.f;
   if (warp == 0 && lane == 0) {
@@ -815,12 +922,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   if (warp == 0) {
     if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
   } else if (warp == 1) {
-    if (lane == 0) mma_issuer<NT>(a, sm, m);
+    if (lane == 0) mma_issuer_a<NT>(a, sm, m);
   } else if (warp == 2) {
-    if (a.dt_bf16) prep_worker<true>(a, m, bi, h);
-    else prep_worker<false>(a, m, bi, h);
+    if (lane == 0) da_producer(a, m, bi, h);
   } else if (warp == 3) {
-    // spare warp
+    if (lane == 0) mma_issuer_b<NT>(a, sm, m);
   } else if (warp < 12) {
     score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
   } else {
@@ -828,6 +934,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   }
   ptx::tc_fence_before();
   __syncthreads();
+#ifdef SSD_TC_DEBUG_TRACE
+  if (a.trace && threadIdx.x == 0 && blockIdx.x < 2048) a.trace[8 * 64 * 16 + 3 * blockIdx.x + 1] = ptx::globaltimer();
+#endif
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(m->tmem_base, TMEM_COLS);
@@ -1014,11 +1123,17 @@ size_t sched_bytes(const ssd_fwd_params_t* p) {
   return p->varlen_states ? (size_t)(8 + 8 * (sched_cap(p) + 1) + 255) / 256 * 256 : 0;
 }
 
+// dt pre-pass output: 1 KB per (batch, head, chunk slot).
+int64_t prep_cap(const ssd_fwd_params_t* p) {
+  return p->varlen_states ? sched_cap(p) : (p->seqlen + QI - 1) / QI;
+}
+size_t prep_bytes(const ssd_fwd_params_t* p) { return (size_t)p->batch * p->nheads * prep_cap(p) * 2 * QI * 4; }
+
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
-  return tc_supported(p) ? 256 + sched_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 : 0) : 0;
+  return tc_supported(p) ? 256 + sched_bytes(p) + prep_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 + 65536 : 0) : 0;
 }
 
-int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 2 : 1; }
+int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : 2; }
 
 int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st) {
   TcArgs a;
@@ -1038,7 +1153,10 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.out = p->out; a.out_x = p->z ? p->out_x : nullptr; a.final_states = p->final_states;
   a.varlen_states = p->varlen_states;
   a.status = (unsigned*)workspace;
-  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256 + sched_bytes(p)) : nullptr;
+  float* prep_out = (float*)((char*)workspace + 256 + sched_bytes(p));
+  a.dtprep = prep_out;
+  a.prep_cap = (int)prep_cap(p);
+  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256 + sched_bytes(p) + prep_bytes(p)) : nullptr;
   typedef void (*KernelFn)(TcArgs);
   static const KernelFn kernels[8] = {
       ssd_fused_tc_kernel<128, false, false>, ssd_fused_tc_kernel<128, false, true>,
@@ -1071,6 +1189,11 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
                                                     p->varlen_states, H * PT * p->dstate);
     a.sched_n = hdr;
     a.sched = sched;
+  }
+  {
+    const dim3 grid((unsigned)a.prep_cap, (unsigned)b, (unsigned)((H + 3) / 4));
+    if (a.dt_bf16) tc_dt_prep_kernel<true><<<grid, 128, 0, st>>>(a, prep_out);
+    else tc_dt_prep_kernel<false><<<grid, 128, 0, st>>>(a, prep_out);
   }
   kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
   const cudaError_t e = cudaGetLastError();
