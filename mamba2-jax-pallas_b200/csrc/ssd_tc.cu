@@ -92,7 +92,7 @@ enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0,
            DA_FREE1, L_FREE, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t X_EMPTY_COUNT = 1 + 4;   // MMA2 commit, SA warps (xs and D x)
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA warps (xs), T warps (D x)
 constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
@@ -675,29 +675,6 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&m->bar[XS_FULL]);
       if (q == 0 || q == 3) TRACE(trole, c, 8);
-      if (a.D_ndim != 0) {
-        // the skip term starts the Y accumulator: Y(c) = D x in f32, MMA2(c) adds S x
-        const int yb = c % G_::YB;
-        if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return;
-        if (q == 0 || q == 3) TRACE(trole, c, 9);
-#pragma unroll 1
-        for (int hx = 0; hx < 2; ++hx) {
-          float v[32];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
-            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack_bf16(wv[j]);
-              v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
-              v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
-            }
-          }
-          ptx::tmem_st32(tmem + COL_Y0 + 128 * yb + 32 * hx, v);
-        }
-        ptx::tmem_st_wait();   // ordered before MMA2(c) by the S_FULL arrival below
-      }
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
       if (q == 0 || q == 3) TRACE(trole, c, 4);
@@ -843,6 +820,38 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
     }
     TRACE(5, c, 2);
+    // The skip term starts the Y accumulator: Y(c) = D x in f32 (row r = TMEM lane r), and
+    // MMA2(c) adds S x.  The Y buffer is free: MMA3(c), which waited for it, is done.
+    {
+      const int xb = c % G_::XST, yb = c % G_::YB;
+      if (a.D_ndim != 0) {
+        if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
+        const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
+#pragma unroll 1
+        for (int hx = 0; hx < 2; ++hx) {
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack_bf16(wv[j]);
+              v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
+              v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
+            }
+          }
+          ptx::tmem_st32(tl + COL_Y0 + 128 * yb + 32 * hx, v);
+        }
+        ptx::tmem_st_wait();
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+        ptx::mbar_arrive(&m->bar[S_FULL]);   // MMA2(c) may accumulate onto Y
+      }
+    }
   }
 }
 
@@ -876,7 +885,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[B_CB], 1);
     ptx::mbar_init(&m->bar[CB_FREE], 8);
     ptx::mbar_init(&m->bar[XS_FULL], 4);
-    ptx::mbar_init(&m->bar[S_FULL], 8);
+    ptx::mbar_init(&m->bar[S_FULL], 12);   // SA and SB scores, T's Y seed
     ptx::mbar_init(&m->bar[ST_READY], 4);
     ptx::mbar_init(&m->bar[B_L], 1);
     ptx::mbar_init(&m->bar[B_Y0], 2);
