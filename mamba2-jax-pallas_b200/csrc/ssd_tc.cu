@@ -88,7 +88,7 @@ struct Geo {
 };
 
 enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB, CB_FREE,
-           XS_FULL, S_FULL, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0, Y_FREE1, DA_READY0, DA_READY1, DA_FREE0,
+           XS_FULL, S_FULL_A, S_FULL_B, Y_SEEDED, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0, Y_FREE1, DA_READY0, DA_READY1, DA_FREE0,
            DA_FREE1, L_FREE, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
@@ -314,16 +314,27 @@ __device__ void mma_issuer_a(const TcArgs& a, uint8_t* sm, Misc* m) {
     TRACE(4, c, 1);
     // MMA2: Y (+)= S . x  (A = bf16 scores in TMEM: tokens 32k..32k+31 in the first 16
     // columns of CB block k; B = x [t][p] MN-major).  With D, Y already holds D x.
-    if (!wait_bar(m, S_FULL, c & 1, a.status)) goto drain;
+    if (!wait_bar(m, S_FULL_A, c & 1, a.status)) goto drain;
+    if (!wait_bar(m, Y_SEEDED, c & 1, a.status)) goto drain;
+    TRACE(4, c, 4);
     if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
     if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
+    TRACE(4, c, 6);
     ptx::tc_fence_after();
     {
       const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
+      // K-steps of score blocks 0 and 1 as soon as every quadrant has written them, then
+      // those of blocks 2 and 3
 #pragma unroll
-      for (int i = 0; i < QI / 16; ++i)
+      for (int i = 0; i < QI / 16; ++i) {
+        if (i == QI / 32) {
+          if (!wait_bar(m, S_FULL_B, c & 1, a.status)) goto drain;
+          TRACE(4, c, 8);
+          ptx::tc_fence_after();
+        }
         ptx::mma_f16_ts(tmem + COL_Y0 + 128 * yb, tmem + COL_CB + 32 * (i >> 1) + 8 * (i & 1),
                         ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, (i > 0 || a.D_ndim != 0) ? 1u : 0u);
+      }
     }
     ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
     ptx::mma_commit(&m->bar[B_Y0 + yb]);
@@ -690,24 +701,32 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       // bf16 scores of this block replace the first 16 of its 32 CB columns (read first)
       const uint32_t tS = tmem + COL_CB + k32 * 32;
       if (k32 > q) {
+        // above the diagonal: zero scores
         const uint32_t zero[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
         ptx::tmem_st16(tS, zero);
-        continue;
+      } else {
+        const int sl = kk == 0 ? sl0 : sl1;
+        const bool fac = block_factored(factor, m->dA[buf], k32);
+        const int lim = k32 == q ? lane : 31;
+        const float* dAc = m->dA[buf] + k32 * 32;
+        const float* wc = m->dt[buf] + k32 * 32;
+        float v[32];
+        uint32_t pk[16];
+        ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);   // one TMEM round trip per block
+        ptx::tmem_ld_wait();
+        if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
+        if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv);
+        else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv);
+        ptx::tmem_st16(tS, pk);
+        if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
       }
-      const int sl = kk == 0 ? sl0 : sl1;
-      const bool fac = block_factored(factor, m->dA[buf], k32);
-      const int lim = k32 == q ? lane : 31;
-      const float* dAc = m->dA[buf] + k32 * 32;
-      const float* wc = m->dt[buf] + k32 * 32;
-      float v[32];
-      uint32_t pk[16];
-      ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);   // one TMEM round trip per block
-      ptx::tmem_ld_wait();
-      if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
-      if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv);
-      else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv);
-      ptx::tmem_st16(tS, pk);
-      if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
+      if (kk == 0) {
+        // blocks 0 and 1 (SA, SB) of this quadrant are in TMEM: MMA2 may start on them
+        ptx::tmem_st_wait();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&m->bar[S_FULL_A]);
+      }
     }
     // rows continuing the previous chunk's sequence read the passed state (rule A9)
     sdec_prev = (seqv == prev_seq) ? __expf(dA) : 0.f;
@@ -716,15 +735,56 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     __syncwarp();
     if (lane == 0) {
       ptx::mbar_arrive(&m->bar[CB_FREE]);
-      ptx::mbar_arrive(&m->bar[S_FULL]);
+      ptx::mbar_arrive(&m->bar[S_FULL_B]);
       ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     }
     if (q == 0 || q == 3) TRACE(trole, c, 7);
+    if (q == 1 || q == 2) TRACE(7, c, 2 * half + (q == 2));
   }
   if (half == 1 && nci > 0) {
     if (!output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, nci - 1, r, sdec_prev)) return;
     if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
   }
+}
+
+// T, after the state update of chunk c: the skip term starts the Y accumulator, Y(c) = D x
+// in f32 (row r = TMEM lane r), and MMA2(c) adds S x.  The Y buffer is free: MMA3(c), done
+// before the state update, waited for it.  Then T releases x(c) and signals Y_SEEDED.
+template <int NT>
+__device__ __forceinline__ bool seed_y(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tl, int c, int r) {
+  using G_ = Geo<NT>;
+  const int lane = r & 31;
+  const int xb = c % G_::XST, yb = c % G_::YB;
+  ptx::tc_fence_after();   // order the TMEM stores after the wait that freed the Y buffer
+  if (a.D_ndim != 0) {
+    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
+    const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
+#pragma unroll 1
+    for (int hx = 0; hx < 2; ++hx) {
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16(wv[j]);
+          v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
+          v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
+        }
+      }
+      ptx::tmem_st32(tl + COL_Y0 + 128 * yb + 32 * hx, v);
+    }
+    ptx::tmem_st_wait();
+  }
+  ptx::tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+    ptx::mbar_arrive(&m->bar[Y_SEEDED]);   // MMA2(c) may accumulate onto Y
+  }
+  TRACE(5, c, 4);
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -820,38 +880,8 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
     }
     TRACE(5, c, 2);
-    // The skip term starts the Y accumulator: Y(c) = D x in f32 (row r = TMEM lane r), and
-    // MMA2(c) adds S x.  The Y buffer is free: MMA3(c), which waited for it, is done.
-    {
-      const int xb = c % G_::XST, yb = c % G_::YB;
-      if (a.D_ndim != 0) {
-        if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
-        const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
-#pragma unroll 1
-        for (int hx = 0; hx < 2; ++hx) {
-          float v[32];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
-            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack_bf16(wv[j]);
-              v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
-              v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
-            }
-          }
-          ptx::tmem_st32(tl + COL_Y0 + 128 * yb + 32 * hx, v);
-        }
-        ptx::tmem_st_wait();
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
-        ptx::mbar_arrive(&m->bar[S_FULL]);   // MMA2(c) may accumulate onto Y
-      }
-    }
+    if (!seed_y<NT>(a, sm, m, tl, c, r)) return;
+
   }
 }
 
@@ -885,7 +915,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[B_CB], 1);
     ptx::mbar_init(&m->bar[CB_FREE], 8);
     ptx::mbar_init(&m->bar[XS_FULL], 4);
-    ptx::mbar_init(&m->bar[S_FULL], 12);   // SA and SB scores, T's Y seed
+    ptx::mbar_init(&m->bar[S_FULL_A], 8);    // SA and SB: score blocks 0, 1
+    ptx::mbar_init(&m->bar[S_FULL_B], 8);    // SA and SB: score blocks 2, 3
+    // T: Y seeded with D x.  Its own barrier: T may seed chunk c+1 before the score warps
+    // arrive for chunk c, and an arrival on S_FULL_A would then complete c's phase early.
+    ptx::mbar_init(&m->bar[Y_SEEDED], 4);
     ptx::mbar_init(&m->bar[ST_READY], 4);
     ptx::mbar_init(&m->bar[B_L], 1);
     ptx::mbar_init(&m->bar[B_Y0], 2);

@@ -399,3 +399,34 @@ def test_tensor_core_path_varlen_states(N, lens, z):
     r()
     torch.cuda.synchronize()
     assert torch.equal(out, out1)
+
+
+@pytest.mark.parametrize("seq", [False, True])
+def test_tensor_core_decay_paths(seq):
+    """Score decays on the fused kernel take three forms per 32-token block: factored
+    (dA non-increasing, block range <= 60), element by element because the range is larger
+    (large |A| dt), and element by element because dA increases (A > 0).  One case mixes
+    all three across heads and compares each with the oracle."""
+    from mamba2_b200.runner import SsdForward
+    lens = [200, 57, 383]
+    L = sum(lens)
+    cfg = S.SsdConfig("t", 1, L, 8, 64, 2, 128, 128, "bf16", has_init=True, return_final=True)
+    inp = S.make_ssd_inputs(cfg, 404)
+    A = np.array([-1.0, -3.0, -40.0, -90.0, 0.05, -0.5, -200.0, -8.0], np.float32)
+    inp["A"] = A
+    s_idx = np.repeat(np.arange(len(lens)), lens)[None].astype(np.int32) if seq else None
+    d = dev_inputs(inp, "bf16")
+    r = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 128, D=d["D"], dt_bias=d["dt_bias"],
+                   initial_states=d["initial_states"], seq_idx=to_dev(s_idx, int32=True), dt_softplus=True,
+                   return_final_states=True)
+    assert r.uses_tc
+    out = r()
+    torch.cuda.synchronize()
+    assert int(r.workspace[:4].view(torch.int32).item()) == 0
+    ref_out, ref_final = R.ssd_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], 128, D=inp["D"],
+                                        dt_bias=inp["dt_bias"], initial_states=inp["initial_states"],
+                                        seq_idx=s_idx, dt_softplus=True, return_final_states=True)
+    assert torch.isfinite(out).all()
+    for h in range(cfg.nheads):
+        assert rel_l2(out[:, :, h], ref_out[:, :, h]) <= TOL["bf16"], h
+        assert rel_l2(r.final[:, h], ref_final[:, h]) <= TOL["bf16"], h
