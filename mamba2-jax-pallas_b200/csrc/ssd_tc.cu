@@ -31,9 +31,9 @@
 //               by the dt pre-pass, bulk-copied into shared memory
 //   warp 3      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
 //   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
-//   warps 8-11  SB: output epilogue E4 of the previous chunk (staged in shared memory and
-//               written by a TMA bulk store), then score column blocks 1 and 3
-//   warps 12-15 T: the state recurrence E3
+//   warps 8-11  SB: score column blocks 1 and 3, then the D x seed of the Y accumulator
+//   warps 12-15 T: the state recurrence E3 and the output epilogue E4 of the previous chunk
+//               (staged in shared memory, written by TMA bulk stores)
 // MMA_L accumulates the chunk's state contribution L_c in its own TMEM columns, so xs and
 // MMA_L do not wait for the state chain.  The bf16 scores go back into TMEM (over the CB
 // columns already read) and MMA2 takes them from there as its A operand.  Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk
@@ -58,19 +58,22 @@ constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
 constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t MISC_BYTES = 2560;
+constexpr uint32_t MISC_BYTES = 2624;
 constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
-constexpr uint32_t COL_CB = 0, COL_Y0 = 128, COL_YI0 = 192;   // Y/Yi buffer b at +128*b
+// TMEM columns: CB / bf16 scores, two buffers (b at 128*b) | Y buffers (64 each) | Yi |
+// f32 state (64 per 128-row half of the state dim).  MMA_L accumulates straight onto the
+// state after T has scaled it by the chunk decay, so the state update needs no column of
+// its own and the CB region can be double-buffered.
+constexpr uint32_t COL_CB0 = 0, COL_Y0 = 256;
 
 // Layout for state dim NT (128 or 256).  C and B stream through a 2-stage ring in 128-column
 // halves (one half per stage), x through its own ring.  Shared memory (from a 1024-aligned
 // base): CB ring | x ring | scores 32 KB | xs 16 KB | bf16 state [n][p] | misc.
-// TMEM columns: CB 128 | Y, Yi (x YB buffers) | f32 state (64 per half) | L (64 per half).
 template <int NT>
 struct Geo {
   static constexpr int NH = NT / 128;               // 128-column halves of the state dim
   static constexpr int XST = NH == 1 ? 2 : 1;       // x buffers
-  static constexpr int YB = NH == 1 ? 2 : 1;        // Y/Yi accumulator buffers
+  static constexpr int YB = NH == 1 ? 2 : 1;        // Y accumulator buffers
   static constexpr uint32_t SZ_H = QI * 128 * 2;    // one half of C or B: 32 KB (two 64-col boxes)
   static constexpr uint32_t SZ_CBST = 2 * SZ_H;     // ring stage: C half + B half
   static constexpr uint32_t SZ_X = QI * PT * 2;     // 16 KB
@@ -81,18 +84,22 @@ struct Geo {
   static constexpr uint32_t OFF_ST = OFF_XS + SZ_X;
   static constexpr uint32_t OFF_MISC = OFF_ST + NT * PT * 2;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
-  static constexpr uint32_t COL_ST = 128 + 128 * YB;
-  static constexpr uint32_t COL_L = COL_ST + 64 * NH;
+  static constexpr uint32_t COL_YI = COL_Y0 + 64 * YB;
+  static constexpr uint32_t COL_ST = COL_YI + 64;
   static_assert(SMEM_BYTES <= SMEM_LAUNCH_BYTES, "shared memory");
-  static_assert(COL_L + 64 * NH <= TMEM_COLS, "tensor memory");
+  static_assert(COL_ST + 64 * NH <= TMEM_COLS, "tensor memory");
 };
 
-enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB, CB_FREE,
-           XS_FULL, S_FULL_A, S_FULL_B, Y_SEEDED, ST_READY, B_L, B_Y0, B_Y1, Y_FREE0, Y_FREE1, DA_READY0, DA_READY1, DA_FREE0,
-           DA_FREE1, L_FREE, OUT_READ, STAGED, DRAIN, NBARS };
+// Barriers.  Every barrier that a role can reach again for a later chunk before another role
+// has consumed the current phase is per buffer (B_CB, CB_FREE, S_FULL_*, Y_SEEDED, B_Y, Y_FREE), so
+// no waiter can see a phase parity two phases late.
+enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB0, B_CB1,
+           CB_FREE0, CB_FREE1, XS_FULL, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1, Y_SEEDED0, Y_SEEDED1,
+           ST_READY, SCALED, B_L, B_Y0, B_Y1, B_YI, Y_FREE0, Y_FREE1, YI_FREE, DA_READY0, DA_READY1, DA_FREE0,
+           DA_FREE1, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA warps (xs), T warps (D x)
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA warps (xs), SB warps (D x)
 constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
@@ -275,70 +282,91 @@ __device__ void da_producer(const TcArgs& a, Misc* m, int bi, int h) {
 
 // ---------------------------------------------------------------------------
 // MMA issuers.  The four MMAs of a chunk have different inputs, and a single issuer in a
-// fixed order would queue the state chain (MMA3, MMA_L) behind MMA1, which waits for the
-// score warps.  So two threads issue, each in chunk order with blocking waits:
-//   A (warp 1, lane 0)  MMA1(c)  CB = C.B^T   after C,B(c) loaded and E2(c-1) done with CB
-//                       MMA2(c)  Y += S.x     after the scores (in TMEM), x(c), Y buffer free
-//   B (warp 3, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, Yi buffer free
-//                       MMA_L(c) L = B^T.xs   after xs(c) and T done with L(c-1)
-// MMA2(c) and MMA1(c+1) share the TMEM columns of the scores; both come from thread A,
-// whose tcgen05.mma execute in issue order.  The C/B ring stage and B_Y each take one
-// commit from both threads; B_CB and X_EMPTY come from A, B_L from B.
+// fixed order would queue the state chain (MMA3, MMA_L) behind the score pipeline.  So two
+// threads issue, each in chunk order with blocking waits:
+//   A (warp 1, lane 0)  MMA1(c)  CB = C.B^T   into CB buffer c%2, after C,B(c) and E2(c-2)
+//                       MMA2(c)  Y (+)= S.x   after the scores of c (in that CB buffer), x(c),
+//                                             the Y seed and the previous output
+//   B (warp 3, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, a free Yi buffer
+//                       MMA_L(c) S += B^T.xs  onto the state T has scaled by the chunk decay
+// With one chunk of C/B per ring stage (N=128), A issues MMA1(c+1) before MMA2(c), so the
+// scores of chunk c+1 can start as soon as those of c are done.  MMA2(c) and MMA1(c+2) share
+// TMEM columns and come from thread A, whose tcgen05.mma execute in issue order.  The C/B
+// ring stage takes one commit from each thread.
 // ---------------------------------------------------------------------------
+template <int NT>
+__device__ __forceinline__ bool issue_mma1(const TcArgs& a, uint8_t* sm, Misc* m, int c) {
+  using G_ = Geo<NT>;
+  constexpr uint32_t ID_CB = ptx::idesc_bf16_f32(128, 128, 0, 0);
+  const uint32_t tmem = m->tmem_base, base = ptx::smem_u32(sm);
+  const int cb = c & 1;
+  for (int hh = 0; hh < G_::NH; ++hh) {
+    const int k = c * G_::NH + hh;
+    if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) return false;
+    // E2(c-2) done with this CB buffer (MMA2(c-2) was issued earlier by this thread)
+    if (hh == 0 && c >= 2 && !wait_bar(m, CB_FREE0 + cb, ((c >> 1) - 1) & 1, a.status)) return false;
+    ptx::tc_fence_after();
+    const uint32_t sC = base + G_::OFF_CB + (k & 1) * G_::SZ_CBST, sB = sC + G_::SZ_H;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t off = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
+      ptx::mma_f16(tmem + COL_CB0 + 128 * cb, ptx::sdesc_sw128(sC + off, 16, 1024),
+                   ptx::sdesc_sw128(sB + off, 16, 1024), ID_CB, (hh > 0 || i > 0) ? 1u : 0u);
+    }
+  }
+  ptx::mma_commit(&m->bar[B_CB0 + cb]);
+  for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
+  TRACE(4, c, 1);
+  return true;
+}
+
+template <int NT>
+__device__ __forceinline__ bool issue_mma2(const TcArgs& a, uint8_t* sm, Misc* m, int c) {
+  using G_ = Geo<NT>;
+  constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
+  const uint32_t tmem = m->tmem_base, base = ptx::smem_u32(sm);
+  const int cb = c & 1, xb = c % G_::XST, yb = c % G_::YB;
+  if (!wait_bar(m, S_FULL_A0 + cb, (c >> 1) & 1, a.status)) return false;
+  if (!wait_bar(m, Y_SEEDED0 + yb, (c / G_::YB) & 1, a.status)) return false;
+  if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
+  if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return false;
+  TRACE(4, c, 4);
+  ptx::tc_fence_after();
+  const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
+  // A = bf16 scores in TMEM (tokens 32k..32k+31 in the first 16 columns of CB block k),
+  // B = x [t][p] MN-major.  K-steps of score blocks 0, 1 first, then those of 2, 3.
+#pragma unroll
+  for (int i = 0; i < QI / 16; ++i) {
+    if (i == QI / 32) {
+      if (!wait_bar(m, S_FULL_B0 + cb, (c >> 1) & 1, a.status)) return false;
+      TRACE(4, c, 8);
+      ptx::tc_fence_after();
+    }
+    ptx::mma_f16_ts(tmem + COL_Y0 + 64 * yb, tmem + COL_CB0 + 128 * cb + 32 * (i >> 1) + 8 * (i & 1),
+                    ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, (i > 0 || a.D_ndim != 0) ? 1u : 0u);
+  }
+  ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
+  ptx::mma_commit(&m->bar[B_Y0 + yb]);
+  TRACE(4, c, 5);
+  return true;
+}
+
 template <int NT>
 __device__ void mma_issuer_a(const TcArgs& a, uint8_t* sm, Misc* m) {
   using G_ = Geo<NT>;
-  const uint32_t tmem = m->tmem_base;
-  const uint32_t base = ptx::smem_u32(sm);
-  constexpr uint32_t ID_CB = ptx::idesc_bf16_f32(128, 128, 0, 0);
-  constexpr uint32_t ID_Y = ptx::idesc_bf16_f32(128, 64, 0, 1);
   const int nci = m->nci;
-  for (int c = 0; c < nci; ++c) {
-    const int yb = c % G_::YB, xb = c % G_::XST;
-    // MMA1: CB = C . B^T, summed over the 128-column halves of the state dim (K-major)
-    for (int hh = 0; hh < G_::NH; ++hh) {
-      const int k = c * G_::NH + hh;
-      if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) goto drain;
-      if (hh == 0 && c > 0 && !wait_bar(m, CB_FREE, (c - 1) & 1, a.status)) goto drain;
-      ptx::tc_fence_after();
-      const uint32_t sC = base + G_::OFF_CB + (k & 1) * G_::SZ_CBST, sB = sC + G_::SZ_H;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t off = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
-        ptx::mma_f16(tmem + COL_CB, ptx::sdesc_sw128(sC + off, 16, 1024), ptx::sdesc_sw128(sB + off, 16, 1024),
-                     ID_CB, (hh > 0 || i > 0) ? 1u : 0u);
-      }
+  if (G_::NH == 1) {
+    if (nci > 0 && !issue_mma1<NT>(a, sm, m, 0)) goto drain;
+    for (int c = 0; c < nci; ++c) {
+      if (c + 1 < nci && !issue_mma1<NT>(a, sm, m, c + 1)) goto drain;
+      if (!issue_mma2<NT>(a, sm, m, c)) goto drain;
     }
-    ptx::mma_commit(&m->bar[B_CB]);
-    for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
-    TRACE(4, c, 1);
-    // MMA2: Y (+)= S . x  (A = bf16 scores in TMEM: tokens 32k..32k+31 in the first 16
-    // columns of CB block k; B = x [t][p] MN-major).  With D, Y already holds D x.
-    if (!wait_bar(m, S_FULL_A, c & 1, a.status)) goto drain;
-    if (!wait_bar(m, Y_SEEDED, c & 1, a.status)) goto drain;
-    TRACE(4, c, 4);
-    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) goto drain;
-    if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
-    TRACE(4, c, 6);
-    ptx::tc_fence_after();
-    {
-      const uint32_t sX = base + G_::OFF_X + xb * G_::SZ_X;
-      // K-steps of score blocks 0 and 1 as soon as every quadrant has written them, then
-      // those of blocks 2 and 3
-#pragma unroll
-      for (int i = 0; i < QI / 16; ++i) {
-        if (i == QI / 32) {
-          if (!wait_bar(m, S_FULL_B, c & 1, a.status)) goto drain;
-          TRACE(4, c, 8);
-          ptx::tc_fence_after();
-        }
-        ptx::mma_f16_ts(tmem + COL_Y0 + 128 * yb, tmem + COL_CB + 32 * (i >> 1) + 8 * (i & 1),
-                        ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, (i > 0 || a.D_ndim != 0) ? 1u : 0u);
-      }
+  } else {
+    // the ring holds one chunk: C/B(c+1) arrive only after chunk c's MMAs, so MMA2(c) first
+    for (int c = 0; c < nci; ++c) {
+      if (!issue_mma1<NT>(a, sm, m, c)) goto drain;
+      if (!issue_mma2<NT>(a, sm, m, c)) goto drain;
     }
-    ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
-    ptx::mma_commit(&m->bar[B_Y0 + yb]);
-    TRACE(4, c, 5);
   }
 drain:
   // wait (bounded) until every MMA this thread issued has completed
@@ -357,40 +385,39 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
   constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
   const int nci = m->nci;
   for (int c = 0; c < nci; ++c) {
-    const int yb = c % G_::YB;
     for (int hh = 0; hh < G_::NH; ++hh) {
       const int k = c * G_::NH + hh;
       if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) goto drain;
     }
-    // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)  -- the state chain
+    // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
-    if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) goto drain;
+    if (c >= 1 && !wait_bar(m, YI_FREE, (c - 1) & 1, a.status)) goto drain;   // output of c-1 read Yi
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
       const uint32_t sC = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t offa = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
-        ptx::mma_f16(tmem + COL_YI0 + 128 * yb, ptx::sdesc_sw128(sC + offa, 16, 1024),
+        ptx::mma_f16(tmem + G_::COL_YI, ptx::sdesc_sw128(sC + offa, 16, 1024),
                      ptx::sdesc_sw128(base + G_::OFF_ST + hh * (128 * 128) + i * 2048, 8192, 1024), ID_YI,
                      (hh > 0 || i > 0) ? 1u : 0u);
       }
     }
+    ptx::mma_commit(&m->bar[B_YI]);
     TRACE(4, c, 2);
-    // MMA_L: L_c = B^T . xs, one 128-row half of the state dim per ring stage
+    // MMA_L: S_{c+1} = (scaled S_c) + B^T . xs, one 128-row half of the state dim per stage
     if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
-    if (c > 0 && !wait_bar(m, L_FREE, (c - 1) & 1, a.status)) goto drain;
+    if (!wait_bar(m, SCALED, c & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
       const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
 #pragma unroll
       for (int i = 0; i < QI / 16; ++i)
-        ptx::mma_f16(tmem + G_::COL_L + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
-                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, i > 0);
+        ptx::mma_f16(tmem + G_::COL_ST + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
+                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, 1u);
     }
-    ptx::mma_commit(&m->bar[B_L]);   // L_c ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
+    ptx::mma_commit(&m->bar[B_L]);   // S_{c+1} ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
     for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
-    ptx::mma_commit(&m->bar[B_Y0 + yb]);
     TRACE(4, c, 3);
   }
 drain:
@@ -509,6 +536,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     for (int k = 0; k < 8; ++k) zq[k] = __ldg(zp + k);
   }
   if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
+  if (!wait_bar(m, B_YI, c & 1, a.status)) return false;
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 8);
   ptx::tc_fence_after();
   // the previous chunk's bulk store must have read the staging buffer (long done by now)
@@ -523,8 +551,8 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float y[32], yi[32];
-    ptx::tmem_ld32(tmem + COL_Y0 + 128 * yb + 32 * half, y);
-    ptx::tmem_ld32(tmem + COL_YI0 + 128 * yb + 32 * half, yi);
+    ptx::tmem_ld32(tmem + COL_Y0 + 64 * yb + 32 * half, y);
+    ptx::tmem_ld32(tmem + G_::COL_YI + 32 * half, yi);
     uint32_t zw[16];
     if (HAS_Z) {
 #pragma unroll
@@ -560,6 +588,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   __syncwarp();
   if (lane == 0) {
     ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
+    ptx::mbar_arrive(&m->bar[YI_FREE]);
     ptx::mbar_arrive(&m->bar[STAGED]);
   }
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 9);
@@ -629,6 +658,47 @@ __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t
   }
 }
 
+// SB, after its scores of chunk c: the skip term starts the Y accumulator, Y(c) = D x in f32
+// (row r = TMEM lane r), and MMA2(c) adds S x.  Y is free once the output of c-1 has read
+// it.  Then SB releases x(c) and signals Y_SEEDED.
+template <int NT>
+__device__ __forceinline__ bool seed_y(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tl, int c, int r) {
+  using G_ = Geo<NT>;
+  const int lane = r & 31;
+  const int xb = c % G_::XST, yb = c % G_::YB;
+  if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return false;
+  ptx::tc_fence_after();   // order the TMEM stores after the wait that freed Y
+  if (a.D_ndim != 0) {
+    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
+    const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
+#pragma unroll 1
+    for (int hx = 0; hx < 2; ++hx) {
+      float v[32];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16(wv[j]);
+          v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
+          v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
+        }
+      }
+      ptx::tmem_st32(tl + COL_Y0 + 64 * yb + 32 * hx, v);
+    }
+    ptx::tmem_st_wait();
+  }
+  ptx::tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+    ptx::mbar_arrive(&m->bar[Y_SEEDED0 + yb]);   // MMA2(c) may accumulate onto Y
+  }
+  TRACE(5, c, 4);
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // score workers SA (warps 4-7, half 0) and SB (warps 8-11, half 1).  Both build score
 // column blocks {half, half+2} of the rows of their quadrant (quadrant q has q+1 non-zero
@@ -645,7 +715,6 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   using G_ = Geo<NT>;
   uint8_t* xs_sm = sm + G_::OFF_XS;
   const int nci = m->nci;
-  float sdec_prev = 0.f;
 #pragma unroll 1
   for (int c = 0; c < nci; ++c) {
     const int buf = c & 1, xb = c % G_::XST;
@@ -654,12 +723,10 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     const int trole = 2 * half + (q == 3);
     (void)trole;
     if (q == 0 || q == 3) TRACE(trole, c, 0);
-    if (half == 1 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, c - 1, r, sdec_prev)) return;
-    int seqv = (r < sp.n) ? 0 : -1, prev_seq = 0, end_seq = 0, sl0 = 0, sl1 = 0;
+    int seqv = (r < sp.n) ? 0 : -1, end_seq = 0, sl0 = 0, sl1 = 0;
     const int last_valid = sp.n - 1;
     if (has_seq) {
       seqv = (r < sp.n) ? seq_at(a, bi, t0 + r) : -1;
-      prev_seq = c == 0 ? 0 : seq_at(a, bi, t0 - 1);
       end_seq = seq_at(a, bi, t0 + last_valid);
       sl0 = seq_at(a, bi, t0 + half * 32 + lane);
       sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
@@ -692,14 +759,15 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     }
 
     // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
-    if (!wait_bar(m, B_CB, c & 1, a.status)) return;
+    const int cb = c & 1;
+    if (!wait_bar(m, B_CB0 + cb, (c >> 1) & 1, a.status)) return;
     if (q == 0 || q == 3) TRACE(trole, c, 6);
     ptx::tc_fence_after();
 #pragma unroll 1
     for (int kk = 0; kk < 2; ++kk) {
       const int k32 = half + 2 * kk;
       // bf16 scores of this block replace the first 16 of its 32 CB columns (read first)
-      const uint32_t tS = tmem + COL_CB + k32 * 32;
+      const uint32_t tS = tmem + COL_CB0 + 128 * cb + k32 * 32;
       if (k32 > q) {
         // above the diagonal: zero scores
         const uint32_t zero[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
@@ -712,7 +780,7 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         const float* wc = m->dt[buf] + k32 * 32;
         float v[32];
         uint32_t pk[16];
-        ptx::tmem_ld32(tmem + COL_CB + k32 * 32, v);   // one TMEM round trip per block
+        ptx::tmem_ld32(tS, v);   // one TMEM round trip per block
         ptx::tmem_ld_wait();
         if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
         if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv);
@@ -725,74 +793,57 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         ptx::tmem_st_wait();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&m->bar[S_FULL_A]);
+        if (lane == 0) ptx::mbar_arrive(&m->bar[S_FULL_A0 + cb]);
       }
     }
-    // rows continuing the previous chunk's sequence read the passed state (rule A9)
-    sdec_prev = (seqv == prev_seq) ? __expf(dA) : 0.f;
     ptx::tmem_st_wait();
     ptx::tc_fence_before();
     __syncwarp();
     if (lane == 0) {
-      ptx::mbar_arrive(&m->bar[CB_FREE]);
-      ptx::mbar_arrive(&m->bar[S_FULL_B]);
+      ptx::mbar_arrive(&m->bar[CB_FREE0 + cb]);
+      ptx::mbar_arrive(&m->bar[S_FULL_B0 + cb]);
       ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
     }
     if (q == 0 || q == 3) TRACE(trole, c, 7);
     if (q == 1 || q == 2) TRACE(7, c, 2 * half + (q == 2));
-  }
-  if (half == 1 && nci > 0) {
-    if (!output_chunk<NT, HAS_Z>(a, sm, m, tmem, bi, h, nci - 1, r, sdec_prev)) return;
-    if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
+    if (half == 1 && !seed_y<NT>(a, sm, m, tmem, c, r)) return;
   }
 }
 
-// T, after the state update of chunk c: the skip term starts the Y accumulator, Y(c) = D x
-// in f32 (row r = TMEM lane r), and MMA2(c) adds S x.  The Y buffer is free: MMA3(c), done
-// before the state update, waited for it.  Then T releases x(c) and signals Y_SEEDED.
-template <int NT>
-__device__ __forceinline__ bool seed_y(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tl, int c, int r) {
-  using G_ = Geo<NT>;
-  const int lane = r & 31;
-  const int xb = c % G_::XST, yb = c % G_::YB;
-  ptx::tc_fence_after();   // order the TMEM stores after the wait that freed the Y buffer
-  if (a.D_ndim != 0) {
-    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
-    const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
-#pragma unroll 1
-    for (int hx = 0; hx < 2; ++hx) {
-      float v[32];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = unpack_bf16(wv[j]);
-          v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
-          v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
-        }
-      }
-      ptx::tmem_st32(tl + COL_Y0 + 128 * yb + 32 * hx, v);
-    }
-    ptx::tmem_st_wait();
+
+// ---------------------------------------------------------------------------
+// state worker T (warps 12-15).  S_{c+1} = decay_c S_c + B^T xs_c, with the product added
+// by MMA_L(c) onto the state T has already scaled in TMEM.  Per chunk c, once MMA_L(c) is
+// done: read S_{c+1}, write its bf16 copy for MMA3(c+1) (and the varlen / final state),
+// store decay_{c+1} S_{c+1} back for MMA_L(c+1), then seed Y(c).  Thread r owns state rows
+// n = r + 128*hh (TMEM lane r, 64 f32 columns per 128-row half).  decay_c is 0 when the
+// chunk-end sequence id changes (state_passing_fwd.py:208-225; the id before the first
+// chunk counts as 0).
+// ---------------------------------------------------------------------------
+template <int NT, bool HAS_SEQ>
+__device__ __forceinline__ bool chunk_decay(const TcArgs& a, Misc* m, int bi, int c, int r, int& prev_end,
+                                            float& decay, float& sdec) {
+  const int buf = c & 1, lane = r & 31;
+  const Span sp = span_at(a, c);
+  const int end_seq = HAS_SEQ ? seq_at(a, bi, (int64_t)sp.t0 + sp.n - 1) : 0;
+  // row r continues the previous chunk's sequence: it reads the passed state (rule A9)
+  bool cont = r < sp.n;
+  if (HAS_SEQ) {
+    const int sr = seq_at(a, bi, (int64_t)sp.t0 + r);
+    const int sp0 = c == 0 ? 0 : seq_at(a, bi, (int64_t)sp.t0 - 1);
+    cont = cont && sr == sp0;
   }
-  ptx::tc_fence_before();
+  if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return false;
+  const float dA_last = m->dA[buf][QI - 1];
+  sdec = cont ? __expf(m->dA[buf][r]) : 0.f;
   __syncwarp();
-  if (lane == 0) {
-    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
-    ptx::mbar_arrive(&m->bar[Y_SEEDED]);   // MMA2(c) may accumulate onto Y
-  }
-  TRACE(5, c, 4);
+  if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
+  decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
+  prev_end = end_seq;
   return true;
 }
 
-// ---------------------------------------------------------------------------
-// state worker T (warps 12-15): S_{c+1} = keep_c exp(dA_last_c) S_c + L_c.  Thread r owns
-// state rows n = r + 128*hh (TMEM lane r, 64 f32 columns per 128-row half) of the state
-// and of L_c.
-// ---------------------------------------------------------------------------
-template <int NT>
+template <int NT, bool HAS_SEQ, bool HAS_Z>
 __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
   using G_ = Geo<NT>;
   const int r = threadIdx.x & 127;
@@ -800,7 +851,12 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
   uint8_t* st_sm = sm + G_::OFF_ST;
   const int64_t bh = (int64_t)bi * a.H + h;
-  // S_0 = initial state (or 0): f32 in TMEM, bf16 operand for MMA3(0)
+  const int nci = m->nci;
+  if (nci <= 0) return;
+  int prev_end = 0;
+  float decay, sd_cur, sd_next = 0.f, sd_prev = 0.f;   // per-row inter-chunk factors of c, c+1, c-1
+  if (!chunk_decay<NT, HAS_SEQ>(a, m, bi, 0, r, prev_end, decay, sd_cur)) return;
+  // S_0 = initial state (or 0): bf16 operand for MMA3(0); decay_0 S_0 in TMEM for MMA_L(0)
 #pragma unroll 1
   for (int seg = 0; seg < 2 * G_::NH; ++seg) {
     const int hh = seg >> 1, half = seg & 1;
@@ -813,76 +869,74 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
           make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
                      pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= decay;
     ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, v);
   }
   ptx::tmem_st_wait();
   ptx::tc_fence_before();
   ptx::fence_proxy_async_smem();
   __syncwarp();
-  if (lane == 0) ptx::mbar_arrive(&m->bar[ST_READY]);
+  if (lane == 0) {
+    ptx::mbar_arrive(&m->bar[ST_READY]);
+    ptx::mbar_arrive(&m->bar[SCALED]);
+  }
 
-  int prev_end = 0;
-  const int nci = m->nci;
 #pragma unroll 1
   for (int c = 0; c < nci; ++c) {
-    const int buf = c & 1;
     const bool more = c + 1 < nci;
-    // chunk decay: 0 when the chunk-end sequence id changes (state_passing_fwd.py:208-225;
-    // the id before the first chunk counts as 0)
+    // this chunk ends packed sequence sp.vslot: the state after it is that sequence's
+    // final state (chunk_state_fwd.py:448-597 computes the same per sequence)
     const Span sp = span_at(a, c);
-    const int end_seq = a.seq_idx ? seq_at(a, bi, (int64_t)sp.t0 + sp.n - 1) : 0;
-    // this chunk ends packed sequence sp.vslot: its state after the chunk is that
-    // sequence's final state (chunk_state_fwd.py:448-597 computes the same per sequence)
     float* const vdst = sp.vslot >= 0 ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
     TRACE(5, c, 0);
-    if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
-    const float dA_last = m->dA[buf][QI - 1];
-    TRACE(5, c, 3);
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
-    const float decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
-    prev_end = end_seq;
-    if (!wait_bar(m, B_L, c & 1, a.status)) return;   // L_c ready, MMA3(c) done with S_c
+    if (more && !chunk_decay<NT, HAS_SEQ>(a, m, bi, c + 1, r, prev_end, decay, sd_next)) return;
+    // MMA3(c) writes Yi after the output of c-1 has read it, so that output comes first
+    if (c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
+    if (!wait_bar(m, B_L, c & 1, a.status)) return;   // S_{c+1} ready, MMA3(c) done with the copy of S_c
     TRACE(5, c, 1);
     ptx::tc_fence_after();
 #pragma unroll 1
     for (int seg = 0; seg < 2 * G_::NH; ++seg) {
       const int hh = seg >> 1, half = seg & 1;
       const int n = hh * 128 + r;
-      float sv[32], lv[32];
+      float sv[32];
       ptx::tmem_ld32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
-      ptx::tmem_ld32(tl + G_::COL_L + 64 * hh + 32 * half, lv);
       ptx::tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = decay * sv[i] + lv[i];
       if (vdst != nullptr) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) vdst[(32 * half + i) * NT + n] = sv[i];
       }
       if (more) {
-        ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
               make_uint4(pack_bf16(sv[8 * j], sv[8 * j + 1]), pack_bf16(sv[8 * j + 2], sv[8 * j + 3]),
                          pack_bf16(sv[8 * j + 4], sv[8 * j + 5]), pack_bf16(sv[8 * j + 6], sv[8 * j + 7]));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[i] *= decay;
+        ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
       } else if (a.final_states) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) a.final_states[(bh * PT + 32 * half + i) * NT + n] = sv[i];
       }
     }
-    if (more) ptx::tmem_st_wait();
-    ptx::tc_fence_before();
-    if (more) ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      ptx::mbar_arrive(&m->bar[L_FREE]);
-      if (more) ptx::mbar_arrive(&m->bar[ST_READY]);
+    if (more) {
+      ptx::tmem_st_wait();
+      ptx::tc_fence_before();
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::mbar_arrive(&m->bar[ST_READY]);
+        ptx::mbar_arrive(&m->bar[SCALED]);
+      }
     }
     TRACE(5, c, 2);
-    if (!seed_y<NT>(a, sm, m, tl, c, r)) return;
-
+    sd_prev = sd_cur;
+    sd_cur = sd_next;
   }
+  if (!output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, nci - 1, r, sd_prev)) return;
+  if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
 }
 
 template <int NT, bool HAS_SEQ, bool HAS_Z>
@@ -904,35 +958,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   const int g = h / (a.H / a.G);
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(&m->bar[CB_FULL0], 1);
-    ptx::mbar_init(&m->bar[CB_FULL1], 1);
+    for (int i = 0; i < NBARS; ++i) ptx::mbar_init(&m->bar[i], 1);   // single arrivals, then the counted ones:
     ptx::mbar_init(&m->bar[CB_EMPTY0], 2);   // one commit from each MMA issuer
     ptx::mbar_init(&m->bar[CB_EMPTY1], 2);
-    ptx::mbar_init(&m->bar[X_FULL0], 1);
-    ptx::mbar_init(&m->bar[X_FULL1], 1);
     ptx::mbar_init(&m->bar[X_EMPTY0], X_EMPTY_COUNT);
     ptx::mbar_init(&m->bar[X_EMPTY1], X_EMPTY_COUNT);
-    ptx::mbar_init(&m->bar[B_CB], 1);
-    ptx::mbar_init(&m->bar[CB_FREE], 8);
+    ptx::mbar_init(&m->bar[CB_FREE0], 8);    // SA and SB done with the CB buffer
+    ptx::mbar_init(&m->bar[CB_FREE1], 8);
     ptx::mbar_init(&m->bar[XS_FULL], 4);
-    ptx::mbar_init(&m->bar[S_FULL_A], 8);    // SA and SB: score blocks 0, 1
-    ptx::mbar_init(&m->bar[S_FULL_B], 8);    // SA and SB: score blocks 2, 3
-    // T: Y seeded with D x.  Its own barrier: T may seed chunk c+1 before the score warps
-    // arrive for chunk c, and an arrival on S_FULL_A would then complete c's phase early.
-    ptx::mbar_init(&m->bar[Y_SEEDED], 4);
-    ptx::mbar_init(&m->bar[ST_READY], 4);
-    ptx::mbar_init(&m->bar[B_L], 1);
-    ptx::mbar_init(&m->bar[B_Y0], 2);
-    ptx::mbar_init(&m->bar[B_Y1], 2);
-    ptx::mbar_init(&m->bar[Y_FREE0], 4);
+    ptx::mbar_init(&m->bar[S_FULL_A0], 8);   // SA and SB: score blocks 0, 1
+    ptx::mbar_init(&m->bar[S_FULL_A1], 8);
+    ptx::mbar_init(&m->bar[S_FULL_B0], 8);   // SA and SB: score blocks 2, 3
+    ptx::mbar_init(&m->bar[S_FULL_B1], 8);
+    ptx::mbar_init(&m->bar[Y_SEEDED0], 4);   // SB: Y seeded with D x
+    ptx::mbar_init(&m->bar[Y_SEEDED1], 4);
+    ptx::mbar_init(&m->bar[ST_READY], 4);    // T: bf16 state copy for MMA3
+    ptx::mbar_init(&m->bar[SCALED], 4);      // T: TMEM state scaled by the chunk decay
+    ptx::mbar_init(&m->bar[Y_FREE0], 4);     // T: output read Y
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
-    ptx::mbar_init(&m->bar[DA_READY0], 1);
-    ptx::mbar_init(&m->bar[DA_READY1], 1);
+    ptx::mbar_init(&m->bar[YI_FREE], 4);     // T: output read Yi
     ptx::mbar_init(&m->bar[DA_FREE0], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[DA_FREE1], DA_FREE_COUNT);
-    ptx::mbar_init(&m->bar[L_FREE], 4);
     ptx::mbar_init(&m->bar[STAGED], 4);
-    ptx::mbar_init(&m->bar[OUT_READ], 1);
     ptx::mbar_init(&m->bar[DRAIN], 2);
     m->abort = 0;
     m->nci = a.sched_n ? *a.sched_n : a.nci;
@@ -973,7 +1020,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   } else if (warp < 12) {
     score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
   } else {
-    state_worker<NT>(a, sm, m, bi, h);
+    state_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h);
   }
   ptx::tc_fence_before();
   __syncthreads();
