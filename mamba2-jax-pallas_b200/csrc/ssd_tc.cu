@@ -95,7 +95,7 @@ struct Geo {
 // no waiter can see a phase parity two phases late.
 enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB0, B_CB1,
            CB_FREE0, CB_FREE1, XS_FULL, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1, Y_SEEDED0, Y_SEEDED1,
-           ST_READY, SCALED, B_L, B_Y0, B_Y1, B_YI, Y_FREE0, Y_FREE1, YI_FREE, DA_READY0, DA_READY1, DA_FREE0,
+           ST_READY, SCALED, B_L, XS_FREE, B_Y0, B_Y1, B_YI, Y_FREE0, Y_FREE1, YI_FREE, DA_READY0, DA_READY1, DA_FREE0,
            DA_FREE1, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
@@ -389,6 +389,20 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
       const int k = c * G_::NH + hh;
       if (!wait_bar(m, CB_FULL0 + (k & 1), (k >> 1) & 1, a.status)) goto drain;
     }
+    // MMA_L first: it does not wait for the previous output
+    // MMA_L: S_{c+1} = (scaled S_c) + B^T . xs, one 128-row half of the state dim per stage
+    if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
+    if (!wait_bar(m, SCALED, c & 1, a.status)) goto drain;
+    ptx::tc_fence_after();
+    for (int hh = 0; hh < G_::NH; ++hh) {
+      const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
+#pragma unroll
+      for (int i = 0; i < QI / 16; ++i)
+        ptx::mma_f16(tmem + G_::COL_ST + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
+                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, 1u);
+    }
+    ptx::mma_commit(&m->bar[XS_FREE]);   // MMA_L(c) done with xs
+    TRACE(4, c, 3);
     // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
     if (c >= 1 && !wait_bar(m, YI_FREE, (c - 1) & 1, a.status)) goto drain;   // output of c-1 read Yi
@@ -405,20 +419,8 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
     }
     ptx::mma_commit(&m->bar[B_YI]);
     TRACE(4, c, 2);
-    // MMA_L: S_{c+1} = (scaled S_c) + B^T . xs, one 128-row half of the state dim per stage
-    if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
-    if (!wait_bar(m, SCALED, c & 1, a.status)) goto drain;
-    ptx::tc_fence_after();
-    for (int hh = 0; hh < G_::NH; ++hh) {
-      const uint32_t sB = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST + G_::SZ_H;
-#pragma unroll
-      for (int i = 0; i < QI / 16; ++i)
-        ptx::mma_f16(tmem + G_::COL_ST + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
-                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, 1u);
-    }
-    ptx::mma_commit(&m->bar[B_L]);   // S_{c+1} ready; MMA3(c) done with the bf16 state, MMA_L(c) with xs
+    ptx::mma_commit(&m->bar[B_L]);   // S_{c+1} ready; MMA3(c) done with the bf16 state
     for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
-    TRACE(4, c, 3);
   }
 drain:
   ptx::mma_commit(&m->bar[DRAIN]);
@@ -742,7 +744,7 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       const float e1 = __expf(m->dA[buf][QI - 1] - (fq ? m->dA[buf][32 * q] : dA)) * m->dt[buf][r];
       const float scale = (end_seq >= 0 && seqv == end_seq) ? e1 : 0.f;
       if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
-      if (c > 0 && !wait_bar(m, B_L, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
+      if (c > 0 && !wait_bar(m, XS_FREE, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
       if (q == 0 || q == 3) TRACE(trole, c, 3);
       const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
