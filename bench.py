@@ -27,6 +27,7 @@ sys.path.insert(0, _REPO)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+from mamba2_b200 import _lib  # noqa: E402
 from mamba2_b200 import synthetic as S  # noqa: E402
 
 N_SETS = 4   # rotated input sets (each > L2 when combined with its output)
@@ -265,7 +266,8 @@ def run_ours(args, cfg, rank, world, device):
     hbm, tfl, peak_kind = _peaks()
     inp = S.make_ssd_inputs(cfg, 1000 + 2 + rank)
     sets = [dev_inputs(inp, cfg, device) for _ in range(N_SETS)]
-    runners = [SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], cfg.chunk_size, **fwd_kwargs(cfg, d))
+    flags = _lib.SSD_FLAG_BF16_MMA if args.bf16_mma else 0
+    runners = [SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], cfg.chunk_size, flags=flags, **fwd_kwargs(cfg, d))
                for d in sets]
     graphs = [r.graph() for r in runners]
     stream = torch.cuda.current_stream()
@@ -297,7 +299,7 @@ def run_ours(args, cfg, rank, world, device):
     def e2e_step(_i):
         dd = {k: (None if v is None else v.to(device, non_blocking=True)) for k, v in host.items()}
         r = mamba_chunk_scan_combined_fwd(dd["x"], dd["dt"], dd["A"], dd["B"], dd["C"], cfg.chunk_size,
-                                          workspace=ws, **fwd_kwargs(cfg, dd))
+                                          workspace=ws, bf16_mma=args.bf16_mma, **fwd_kwargs(cfg, dd))
         if cfg.return_final:
             out_h.copy_(r[0], non_blocking=True)
             fin_h.copy_(r[1], non_blocking=True)
@@ -327,11 +329,12 @@ def run_ours(args, cfg, rank, world, device):
     line = {"metric": "SSD layer fwd tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "bf16" else "f32",
+            "vs_baseline": None, "dtype": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else "f32",
             "data": "synthetic",
             "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch, "seqlen": cfg.seqlen,
                        "nheads": cfg.nheads, "headdim": cfg.headdim, "ngroups": cfg.ngroups,
                        "dstate": cfg.dstate, "chunk_size": cfg.chunk_size, "input_dtype": cfg.dtype,
+                       "mma_operands": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else "none (fp32 FFMA)",
                        "parallelism": f"batch-sharded x{world}, no collective",
                        "l2": f"{N_SETS} rotated input sets, each step's inputs+outputs > L2"},
             "roofline": {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
@@ -439,6 +442,9 @@ def main():
     ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--bf16-mma", action="store_true",
+                    help="fp32 configs: bf16 MMA operands on the tensor-core path (the reference's Pallas "
+                         "behaviour for fp32 inputs) instead of exact fp32")
     ap.add_argument("--override", action="append", default=[],
                     help="key=value on the config (e.g. batch=32) for small profiling cases")
     args = ap.parse_args()

@@ -85,6 +85,11 @@ typedef struct ssd_fwd_params {
 #define SSD_FLAG_FORCE_SIMT   1  /* use the fp32 CUDA-core pipeline even for bf16 inputs */
 #define SSD_FLAG_ROUND_STATES 2  /* round passed chunk states to the input dtype before
                                     chunk_scan, as ssd_combined.py:140 does */
+#define SSD_FLAG_BF16_MMA     4  /* fp32 inputs: round x, B, C (and z) to bf16 into the
+                                    workspace and run the tensor-core pipeline, as the
+                                    reference's Pallas kernels do for fp32 inputs (bf16 MMA
+                                    operands, fp32 accumulation); without it fp32 inputs run
+                                    exact fp32 on the CUDA cores */
 
 /* Bytes of device workspace ssd_combined_fwd needs for these params. */
 size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p);

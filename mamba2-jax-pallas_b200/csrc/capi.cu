@@ -1,5 +1,6 @@
 // C ABI entry points (include/ssd_b200.h): argument validation, workspace carving and
 // stage orchestration.  No entry point allocates device memory or blocks the host.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -10,6 +11,7 @@
 #include "ssd_tc.h"
 
 namespace {
+using ssd::bf16;
 
 thread_local char g_err[512] = "";
 
@@ -79,6 +81,66 @@ int validate_fwd(const ssd_fwd_params_t* p) {
   return SSD_OK;
 }
 
+// fp32 -> bf16 copies of x, B, C (and z) for SSD_FLAG_BF16_MMA: one launch, blockIdx.y picks
+// the tensor, each thread converts 4 consecutive elements per step.
+struct ConvJob {
+  const float* src[4];
+  bf16* dst[4];
+  int64_t n[4];
+};
+
+__global__ void __launch_bounds__(256) to_bf16_kernel(const __grid_constant__ ConvJob j) {
+  const int t = blockIdx.y;
+  const float* __restrict__ src = j.src[t];
+  bf16* __restrict__ dst = j.dst[t];
+  const int64_t n = j.n[t];
+  if (!src) return;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
+    if (i + 4 <= n && ((reinterpret_cast<uintptr_t>(src + i) & 15) == 0)) {
+      const float4 v = *reinterpret_cast<const float4*>(src + i);
+      __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+      reinterpret_cast<__nv_bfloat162*>(dst + i)[0] = a;
+      reinterpret_cast<__nv_bfloat162*>(dst + i)[1] = b;
+    } else {
+      for (int64_t k = i; k < i + 4 && k < n; ++k) dst[k] = __float2bfloat16_rn(src[k]);
+    }
+  }
+}
+
+// SSD_FLAG_BF16_MMA: the bf16 copies sit at the head of the workspace (256-byte aligned
+// each); `q` is the params with the inputs redirected there and dtype bf16.
+struct Bf16Plan {
+  bool on;
+  ssd_fwd_params_t q;
+  size_t off_x, off_b, off_c, off_z, bytes;
+};
+
+Bf16Plan plan_bf16(const ssd_fwd_params_t* p, const void* workspace) {
+  Bf16Plan r;
+  memset(&r, 0, sizeof(r));
+  if (!(p->flags & SSD_FLAG_BF16_MMA) || p->dtype != SSD_DTYPE_F32 || (p->flags & SSD_FLAG_FORCE_SIMT)) return r;
+  const size_t nx = (size_t)p->batch * p->seqlen * p->nheads * p->headdim;
+  const size_t nb = (size_t)p->batch * p->seqlen * p->ngroups * p->dstate;
+  size_t off = 0;
+  r.off_x = off; off += align256(nx * 2);
+  r.off_b = off; off += align256(nb * 2);
+  r.off_c = off; off += align256(nb * 2);
+  r.off_z = off; if (p->z) off += align256(nx * 2);
+  r.bytes = off;
+  r.q = *p;
+  r.q.dtype = SSD_DTYPE_BF16;
+  r.q.flags &= ~SSD_FLAG_BF16_MMA;
+  // for sizing without a workspace, any 256-aligned address stands in
+  const char* base = workspace ? (const char*)workspace : reinterpret_cast<const char*>(uintptr_t(256));
+  r.q.x = base + r.off_x;
+  r.q.B = base + r.off_b;
+  r.q.C = base + r.off_c;
+  r.q.z = p->z ? base + r.off_z : nullptr;
+  r.on = ssd::tc_supported(&r.q);
+  return r;
+}
+
 }  // namespace
 
 namespace ssd {
@@ -93,17 +155,22 @@ int ssd_abi_version(void) { return SSD_B200_ABI_VERSION; }
 
 size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p) {
   if (!p) return 0;
+  const Bf16Plan bp = plan_bf16(p, nullptr);
+  if (bp.on) return bp.bytes + ssd::tc_workspace_bytes(&bp.q);
   const size_t tc = ssd::tc_workspace_bytes(p);
   const size_t simt = plan_ws(p).total;
   return tc > simt ? tc : simt;
 }
 
 int ssd_combined_uses_tensor_cores(const ssd_fwd_params_t* p) {
-  return (p && validate_fwd(p) == SSD_OK && !(p->flags & SSD_FLAG_FORCE_SIMT) && ssd::tc_supported(p)) ? 1 : 0;
+  if (!p || validate_fwd(p) != SSD_OK || (p->flags & SSD_FLAG_FORCE_SIMT)) return 0;
+  return (plan_bf16(p, nullptr).on || ssd::tc_supported(p)) ? 1 : 0;
 }
 
 int ssd_combined_num_launches(const ssd_fwd_params_t* p) {
   if (!p || validate_fwd(p) != SSD_OK) return 0;
+  const Bf16Plan bp = plan_bf16(p, nullptr);
+  if (bp.on) return 1 + ssd::tc_num_launches(&bp.q);
   if (ssd_combined_uses_tensor_cores(p)) return ssd::tc_num_launches(p);
   return 5 + (p->varlen_states ? 1 : 0);
 }
@@ -118,6 +185,25 @@ int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspac
   if (!workspace || workspace_bytes < need)
     return fail(SSD_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", need, workspace_bytes);
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(SSD_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+
+  // fp32 inputs with bf16 MMA operands: convert, then the tensor-core pipeline
+  const Bf16Plan bp = plan_bf16(p, workspace);
+  if (bp.on) {
+    char* ws = (char*)workspace;
+    ConvJob j;
+    memset(&j, 0, sizeof(j));
+    const int64_t nx = p->batch * p->seqlen * p->nheads * p->headdim;
+    const int64_t nb = p->batch * p->seqlen * p->ngroups * p->dstate;
+    j.src[0] = (const float*)p->x; j.dst[0] = (bf16*)(ws + bp.off_x); j.n[0] = nx;
+    j.src[1] = (const float*)p->B; j.dst[1] = (bf16*)(ws + bp.off_b); j.n[1] = nb;
+    j.src[2] = (const float*)p->C; j.dst[2] = (bf16*)(ws + bp.off_c); j.n[2] = nb;
+    if (p->z) { j.src[3] = (const float*)p->z; j.dst[3] = (bf16*)(ws + bp.off_z); j.n[3] = nx; }
+    const int64_t most = nx > nb ? nx : nb;
+    const unsigned gx = (unsigned)std::min<int64_t>((most / 4 + 255) / 256, 4 * 148);
+    to_bf16_kernel<<<dim3(gx, 4), 256, 0, st>>>(j);
+    if ((s = cuda_status(cudaGetLastError(), "to_bf16_kernel"))) return s;
+    return ssd::tc_combined_fwd(&bp.q, ws + bp.bytes, st);
+  }
 
   // Tensor-core pipeline for bf16 inputs when the shape is one it covers.
   if (!(p->flags & SSD_FLAG_FORCE_SIMT) && ssd::tc_supported(p)) {

@@ -21,6 +21,7 @@ SSD_DTYPE_F32 = 0
 SSD_DTYPE_BF16 = 1
 SSD_FLAG_FORCE_SIMT = 1
 SSD_FLAG_ROUND_STATES = 2
+SSD_FLAG_BF16_MMA = 4
 SSD_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 STATUS_NAMES = {0: "SSD_OK", 1: "SSD_ERR_INVALID_ARG", 2: "SSD_ERR_UNSUPPORTED",

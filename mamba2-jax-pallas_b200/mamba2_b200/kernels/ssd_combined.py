@@ -65,7 +65,7 @@ def mamba_chunk_scan_combined_fwd(
     seq_idx=None, cu_seqlens=None, dt_softplus: bool = False,
     dt_limit: tuple = (0.0, float("inf")), return_final_states: bool = False,
     return_varlen_states: bool = False, *, round_states: bool = False,
-    force_simt: bool = False, return_out_x: bool = False, workspace=None,
+    force_simt: bool = False, bf16_mma: bool = False, return_out_x: bool = False, workspace=None,
 ):
     """Mamba2 SSD chunked-scan forward (reference ``ssd_combined.py:46-203``).
 
@@ -73,7 +73,9 @@ def mamba_chunk_scan_combined_fwd(
     ``(out, final_states, varlen_states)`` exactly as ``ssd_combined.py:194-203``.
     Keyword-only extensions: ``round_states`` rounds the passed chunk states to the input
     dtype before the output stage (the reference does, ``ssd_combined.py:140``);
-    ``force_simt`` selects the fp32 CUDA-core pipeline; ``return_out_x`` appends the
+    ``force_simt`` selects the fp32 CUDA-core pipeline; ``bf16_mma`` runs fp32 inputs on the
+    tensor-core pipeline with bf16 MMA operands (the reference's Pallas kernels do the same
+    for fp32 inputs), instead of exact fp32 on the CUDA cores; ``return_out_x`` appends the
     pre-gate output; ``workspace`` is an optional preallocated uint8 CUDA tensor.
     """
     if not return_varlen_states:
@@ -81,7 +83,8 @@ def mamba_chunk_scan_combined_fwd(
     elif cu_seqlens is None:
         raise ValueError("return_varlen_states requires cu_seqlens")
     flags = (_lib.SSD_FLAG_ROUND_STATES if round_states else 0) | \
-            (_lib.SSD_FLAG_FORCE_SIMT if force_simt else 0)
+            (_lib.SSD_FLAG_FORCE_SIMT if force_simt else 0) | \
+            (_lib.SSD_FLAG_BF16_MMA if bf16_mma else 0)
     p, t = _fwd_params(x, dt, A, B, C, chunk_size, D, z, dt_bias, initial_states, seq_idx,
                        cu_seqlens, dt_softplus, dt_limit, flags)
     b, L, H, P = x.shape

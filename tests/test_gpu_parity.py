@@ -430,3 +430,28 @@ def test_tensor_core_decay_paths(seq):
     for h in range(cfg.nheads):
         assert rel_l2(out[:, :, h], ref_out[:, :, h]) <= TOL["bf16"], h
         assert rel_l2(r.final[:, h], ref_final[:, h]) <= TOL["bf16"], h
+
+
+@pytest.mark.parametrize("z", [False, True])
+def test_fp32_inputs_with_bf16_mma(z):
+    """SSD_FLAG_BF16_MMA: fp32 inputs rounded to bf16 operands on the tensor-core path (the
+    reference's Pallas behaviour for fp32 inputs), held to the bf16 tolerance; without the
+    flag the same inputs take the exact fp32 path."""
+    from mamba2_b200 import _lib
+    from mamba2_b200.runner import SsdForward
+    cfg = S.SsdConfig("f32mma", 1, 640, 8, 64, 1, 128, 256, "f32", has_z=z, has_init=True, return_final=True)
+    inp = S.make_ssd_inputs(cfg, 51)
+    d = dev_inputs(inp, "f32")
+    kw = dict(D=d["D"], z=d["z"], dt_bias=d["dt_bias"], initial_states=d["initial_states"], dt_softplus=True,
+              return_final_states=True)
+    exact = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 256, **kw)
+    fast = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 256, flags=_lib.SSD_FLAG_BF16_MMA, **kw)
+    assert not exact.uses_tc and fast.uses_tc
+    assert fast.launches_per_step == 3   # conversion, dt pre-pass, fused kernel
+    out = fast()
+    torch.cuda.synchronize()
+    ref_out, ref_final = R.ssd_combined(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"], 256, D=inp["D"],
+                                        z=inp["z"], dt_bias=inp["dt_bias"], initial_states=inp["initial_states"],
+                                        dt_softplus=True, return_final_states=True)
+    assert rel_l2(out, ref_out) <= TOL["bf16"]
+    assert rel_l2(fast.final, ref_final) <= TOL["bf16"]
