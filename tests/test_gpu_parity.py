@@ -455,3 +455,31 @@ def test_fp32_inputs_with_bf16_mma(z):
                                         dt_softplus=True, return_final_states=True)
     assert rel_l2(out, ref_out) <= TOL["bf16"]
     assert rel_l2(fast.final, ref_final) <= TOL["bf16"]
+
+
+@pytest.mark.parametrize("key", ["c2", "c3"])
+def test_full_size_scaling_and_determinism(key):
+    """At the full BASELINE sizes (too large for the oracle): without z the forward is linear
+    in (x, initial state), and scaling both by 2 is exact at every rounding point (bf16
+    operands, fp32 accumulation), so out(2x, 2 h0) must equal 2 out(x, h0) bit for bit, as
+    must the final and varlen states.  A second run must also be bitwise identical."""
+    from mamba2_b200 import mamba_chunk_scan_combined_fwd
+    cfg = S.CONFIGS[key]
+    inp = S.make_ssd_inputs(cfg, 4242)
+    d = dev_inputs(inp, cfg.dtype)
+    varlen = d["cu_seqlens"] is not None
+    init = d["initial_states"] if d["initial_states"] is not None else None
+
+    def run(scale):
+        return mamba_chunk_scan_combined_fwd(
+            d["x"] * scale, d["dt"], d["A"], d["B"], d["C"], cfg.chunk_size, D=d["D"], dt_bias=d["dt_bias"],
+            initial_states=None if init is None else init * scale, seq_idx=d["seq_idx"],
+            cu_seqlens=d["cu_seqlens"], dt_softplus=True, return_final_states=True,
+            return_varlen_states=varlen)
+
+    r1, r1b, r2 = run(1.0), run(1.0), run(2.0)
+    torch.cuda.synchronize()
+    for a_, b_, c_ in zip(r1, r1b, r2):
+        assert torch.isfinite(a_).all()
+        assert torch.equal(a_, b_)
+        assert torch.equal(c_, 2 * a_)
