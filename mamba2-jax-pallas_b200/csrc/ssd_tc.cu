@@ -10,12 +10,13 @@
 // Per chunk c (t = token in chunk, m = output row, n = state dim, p = head dim):
 //   MMA1  CB[m][t]  = C[m][:] . B[t][:]                 (M=128, N=128, K=N)   TMEM
 //   E2    S[m][t]   = CB[m][t] exp(dA_m - dA_t) dt_t    (t <= m, same seq)    -> TMEM bf16
-//   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM (2 bufs)
-//   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM (2 bufs)
+//         S[m][m]  += D                                 (the skip term D x rides on MMA2)
+//   MMA2  Y[m][p]   = S[m][:] . x[:][p]                 (M=128, N=64,  K=128) TMEM
+//   MMA3  Yi[m][p]  = C[m][:] . S_c[p][:]               (M=128, N=64,  K=N)   TMEM (2 bufs at N=128)
 //   E1    xs[t][p]  = x[t][p] exp(dA_last - dA_t) dt_t  (chunk-end seq only)  -> smem bf16
 //   MMA_L Lt[n][p]  = B[:][n] . xs[:][p]                (M=N,   N=64,  K=128) TMEM
 //   E3    S_{c+1}   = keep_c exp(dA_last_c) S_c + Lt    (TMEM f32)  -> bf16 smem for MMA3
-//   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi + D x ; * silu(z)
+//   E4    out[m][p] = Y + exp(dA_m) [seq_m == prev] Yi ; * silu(z)
 // Decay factors come from differences of the in-chunk cumulative sums, as in
 // ssd_naive.py:264-268, never from exp(dA_m) * exp(-dA_t) over a whole chunk.  Within one
 // 32-token column block k they factor as exp(dA_m - dA_{32k}) * exp(dA_{32k} - dA_t) when
@@ -30,8 +31,8 @@
 //   warp 2      dA producer (lane 0): the chunk's cumulative dA and decay factors, computed
 //               by the dt pre-pass, bulk-copied into shared memory
 //   warp 3      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
-//   warps 4-7   SA: xs = x * scale, score column blocks 0 and 2 of each row quadrant
-//   warps 8-11  SB: score column blocks 1 and 3, then the D x seed of the Y accumulator
+//   warps 4-7   SA: xs columns 0-31, score column blocks 0 and 2 of each row quadrant
+//   warps 8-11  SB: xs columns 32-63, score column blocks 1 and 3
 //   warps 12-15 T: the state recurrence E3 and the output epilogue E4 of the previous chunk
 //               (staged in shared memory, written by TMA bulk stores)
 // MMA_L accumulates the chunk's state contribution L_c in its own TMEM columns, so xs and
@@ -60,11 +61,17 @@ constexpr int NTHREADS = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MISC_BYTES = 2624;
 constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
-// TMEM columns: CB / bf16 scores, two buffers (b at 128*b) | Y buffers (64 each) | Yi |
+// TMEM columns: CB / bf16 scores, two buffers (b at 128*b) | Y buffers | Yi buffers (64 each) |
 // f32 state (64 per 128-row half of the state dim).  MMA_L accumulates straight onto the
 // state after T has scaled it by the chunk decay, so the state update needs no column of
 // its own and the CB region can be double-buffered.
 constexpr uint32_t COL_CB0 = 0, COL_Y0 = 256;
+// Yi buffers at N = 128 (Y gets the other of three 64-column slots).  Two Yi buffers let
+// the output of c-1 follow the state copy of c, but MMA2(c) must then wait for it: slower
+// on long single sequences, faster on many short CTAs.  Default one.
+#ifndef SSD_TC_YI_BUFS
+#define SSD_TC_YI_BUFS 1
+#endif
 
 // Layout for state dim NT (128 or 256).  C and B stream through a 2-stage ring in 128-column
 // halves (one half per stage), x through its own ring.  Shared memory (from a 1024-aligned
@@ -73,7 +80,9 @@ template <int NT>
 struct Geo {
   static constexpr int NH = NT / 128;               // 128-column halves of the state dim
   static constexpr int XST = NH == 1 ? 2 : 1;       // x buffers
-  static constexpr int YB = NH == 1 ? 2 : 1;        // Y accumulator buffers
+  static constexpr int YIB = NH == 1 ? SSD_TC_YI_BUFS : 1;   // Yi accumulator buffers
+  static constexpr int YB = NH == 1 ? 3 - YIB : 1;           // Y accumulator buffers
+  static constexpr uint32_t COL_YI0 = COL_Y0 + 64 * YB;
   static constexpr uint32_t SZ_H = QI * 128 * 2;    // one half of C or B: 32 KB (two 64-col boxes)
   static constexpr uint32_t SZ_CBST = 2 * SZ_H;     // ring stage: C half + B half
   static constexpr uint32_t SZ_X = QI * PT * 2;     // 16 KB
@@ -84,22 +93,21 @@ struct Geo {
   static constexpr uint32_t OFF_ST = OFF_XS + SZ_X;
   static constexpr uint32_t OFF_MISC = OFF_ST + NT * PT * 2;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
-  static constexpr uint32_t COL_YI = COL_Y0 + 64 * YB;
-  static constexpr uint32_t COL_ST = COL_YI + 64;
+  static constexpr uint32_t COL_ST = COL_YI0 + 64 * YIB;
   static_assert(SMEM_BYTES <= SMEM_LAUNCH_BYTES, "shared memory");
   static_assert(COL_ST + 64 * NH <= TMEM_COLS, "tensor memory");
 };
 
 // Barriers.  Every barrier that a role can reach again for a later chunk before another role
-// has consumed the current phase is per buffer (B_CB, CB_FREE, S_FULL_*, Y_SEEDED, B_Y, Y_FREE), so
+// has consumed the current phase is per buffer (B_CB, CB_FREE, S_FULL_*, B_YI, YI_FREE), so
 // no waiter can see a phase parity two phases late.
 enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB0, B_CB1,
-           CB_FREE0, CB_FREE1, XS_FULL, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1, Y_SEEDED0, Y_SEEDED1,
-           ST_READY, SCALED, B_L, XS_FREE, B_Y0, B_Y1, B_YI, Y_FREE0, Y_FREE1, YI_FREE, DA_READY0, DA_READY1, DA_FREE0,
+           CB_FREE0, CB_FREE1, XS_FULL, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1,
+           ST_READY, SCALED, B_L, XS_FREE, B_Y0, B_Y1, B_YI0, B_YI1, Y_FREE0, Y_FREE1, YI_FREE0, YI_FREE1, DA_READY0, DA_READY1, DA_FREE0,
            DA_FREE1, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA warps (xs), SB warps (D x)
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA and SB warps (their halves of xs)
 constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
@@ -107,7 +115,7 @@ struct Misc {
   // Per token t of 32-token block k: w_t = exp(dA_{32k} - dA_t) dt_t when block k is
   // factored (block_factored), else the processed dt_t.
   float dt[2][QI];
-  float Dv[PT];         // skip coefficient per head-dim column (0 without D)
+  float Dh;             // skip coefficient of the head (0 without D)
   uint64_t bar[NBARS];
   uint32_t tmem_base;
   int nci;              // chunks of this CTA's walk (from the schedule when there is one)
@@ -295,8 +303,8 @@ __device__ void da_producer(const TcArgs& a, Misc* m, int bi, int h) {
 // fixed order would queue the state chain (MMA3, MMA_L) behind the score pipeline.  So two
 // threads issue, each in chunk order with blocking waits:
 //   A (warp 1, lane 0)  MMA1(c)  CB = C.B^T   into CB buffer c%2, after C,B(c) and E2(c-2)
-//                       MMA2(c)  Y (+)= S.x   after the scores of c (in that CB buffer), x(c),
-//                                             the Y seed and the previous output
+//                       MMA2(c)  Y = S.x      after the scores of c (in that CB buffer), x(c)
+//                                             and the output of c-1
 //   B (warp 3, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, a free Yi buffer
 //                       MMA_L(c) S += B^T.xs  onto the state T has scaled by the chunk decay
 // With one chunk of C/B per ring stage (N=128), A issues MMA1(c+1) before MMA2(c), so the
@@ -337,8 +345,8 @@ __device__ __forceinline__ bool issue_mma2(const TcArgs& a, uint8_t* sm, Misc* m
   const uint32_t tmem = m->tmem_base, base = ptx::smem_u32(sm);
   const int cb = c & 1, xb = c % G_::XST, yb = c % G_::YB;
   if (!wait_bar(m, S_FULL_A0 + cb, (c >> 1) & 1, a.status)) return false;
-  if (!wait_bar(m, Y_SEEDED0 + yb, (c / G_::YB) & 1, a.status)) return false;
   if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
+  // the output of c-YB has read this Y buffer
   if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return false;
   TRACE(4, c, 4);
   ptx::tc_fence_after();
@@ -353,7 +361,7 @@ __device__ __forceinline__ bool issue_mma2(const TcArgs& a, uint8_t* sm, Misc* m
       ptx::tc_fence_after();
     }
     ptx::mma_f16_ts(tmem + COL_Y0 + 64 * yb, tmem + COL_CB0 + 128 * cb + 32 * (i >> 1) + 8 * (i & 1),
-                    ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, (i > 0 || a.D_ndim != 0) ? 1u : 0u);
+                    ptx::sdesc_sw128(sX + i * 2048, 8192, 1024), ID_Y, i > 0 ? 1u : 0u);
   }
   ptx::mma_commit(&m->bar[X_EMPTY0 + xb]);
   ptx::mma_commit(&m->bar[B_Y0 + yb]);
@@ -415,19 +423,20 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
     TRACE(4, c, 3);
     // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
-    if (c >= 1 && !wait_bar(m, YI_FREE, (c - 1) & 1, a.status)) goto drain;   // output of c-1 read Yi
+    // the output of c-YIB has read this Yi buffer
+    if (c >= G_::YIB && !wait_bar(m, YI_FREE0 + c % G_::YIB, ((c / G_::YIB) - 1) & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
       const uint32_t sC = base + G_::OFF_CB + ((c * G_::NH + hh) & 1) * G_::SZ_CBST;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const uint32_t offa = (i >> 2) * (G_::SZ_H / 2) + (i & 3) * 32;
-        ptx::mma_f16(tmem + G_::COL_YI, ptx::sdesc_sw128(sC + offa, 16, 1024),
+        ptx::mma_f16(tmem + G_::COL_YI0 + 64 * (c % G_::YIB), ptx::sdesc_sw128(sC + offa, 16, 1024),
                      ptx::sdesc_sw128(base + G_::OFF_ST + hh * (128 * 128) + i * 2048, 8192, 1024), ID_YI,
                      (hh > 0 || i > 0) ? 1u : 0u);
       }
     }
-    ptx::mma_commit(&m->bar[B_YI]);
+    ptx::mma_commit(&m->bar[B_YI0 + c % G_::YIB]);
     TRACE(4, c, 2);
     ptx::mma_commit(&m->bar[B_L]);   // S_{c+1} ready; MMA3(c) done with the bf16 state
     for (int hh = 0; hh < G_::NH; ++hh) ptx::mma_commit(&m->bar[CB_EMPTY0 + ((c * G_::NH + hh) & 1)]);
@@ -524,7 +533,7 @@ __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__
   reinterpret_cast<float4*>(o + QI)[lane] = make_float4(w[0], w[1], w[2], w[3]);
 }
 
-// Output epilogue of chunk c (run by SB): out = Y + sdec Yi + D x, z gate.  Row r is
+// Output epilogue of chunk c (run by T): out = Y + sdec Yi, z gate (Y holds D x).  Row r is
 // staged as f32 in the (free) score buffer as two 128B-swizzled [128][32] boxes and
 // written by one TMA bulk store per box, so global writes are full lines.  The inner
 // loops carry no data-dependent branches (each costs tens of cycles when unrolled).
@@ -532,7 +541,7 @@ template <int NT, bool HAS_Z>
 __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tmem, int bi, int h, int c, int r,
                              float sdec) {
   using G_ = Geo<NT>;
-  const int yb = c % G_::YB;
+  const int yb = c % G_::YB, yib = c % G_::YIB;
   const int lane = r & 31;
   const Span sp = span_at(a, c);
   const int64_t pos = (int64_t)sp.t0 + r;
@@ -548,7 +557,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     for (int k = 0; k < 8; ++k) zq[k] = __ldg(zp + k);
   }
   if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
-  if (!wait_bar(m, B_YI, c & 1, a.status)) return false;
+  if (!wait_bar(m, B_YI0 + yib, (c / G_::YIB) & 1, a.status)) return false;
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 8);
   ptx::tc_fence_after();
   // the previous chunk's bulk store must have read the staging buffer (long done by now)
@@ -564,7 +573,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   for (int half = 0; half < 2; ++half) {
     float y[32], yi[32];
     ptx::tmem_ld32(tmem + COL_Y0 + 64 * yb + 32 * half, y);
-    ptx::tmem_ld32(tmem + G_::COL_YI + 32 * half, yi);
+    ptx::tmem_ld32(tmem + G_::COL_YI0 + 64 * yib + 32 * half, yi);
     uint32_t zw[16];
     if (HAS_Z) {
 #pragma unroll
@@ -575,7 +584,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     }
     ptx::tmem_ld_wait();
 #pragma unroll
-    for (int k = 0; k < 32; ++k) y[k] = fmaf(sdec, yi[k], y[k]);   // Y already holds D x
+    for (int k = 0; k < 32; ++k) y[k] = fmaf(sdec, yi[k], y[k]);   // Y already holds D x (diagonal)
     if (HAS_Z) {
       if (out_x != nullptr && valid) {
 #pragma unroll
@@ -600,7 +609,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   __syncwarp();
   if (lane == 0) {
     ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
-    ptx::mbar_arrive(&m->bar[YI_FREE]);
+    ptx::mbar_arrive(&m->bar[YI_FREE0 + yib]);
     ptx::mbar_arrive(&m->bar[STAGED]);
   }
   if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 9);
@@ -627,7 +636,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
 // diagonal block, 31 below it).
 template <bool HAS_SEQ>
 __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (&pk)[16], float u, const float* wc,
-                                                int lim, int sl, int seqv) {
+                                                int lim, int sl, int seqv, int dcol, float dg) {
 #pragma unroll
   for (int i4 = 0; i4 < 8; ++i4) {
     const float4 w4 = *reinterpret_cast<const float4*>(wc + 4 * i4);
@@ -642,7 +651,7 @@ __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (
         const int st = __shfl_sync(0xffffffffu, sl, i);
         ok = ok && (st == seqv);
       }
-      o[j] = ok ? v[i] * (u * wv[j]) : 0.f;
+      o[j] = (ok ? v[i] * (u * wv[j]) : 0.f) + (i == dcol ? dg : 0.f);
     }
     pk[2 * i4] = pack_bf16(o[0], o[1]);
     pk[2 * i4 + 1] = pack_bf16(o[2], o[3]);
@@ -653,7 +662,7 @@ __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (
 // heads with large |A| dt): exp(dA_r - dA_t) dt_t per element.
 template <bool HAS_SEQ>
 __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
-                                                  const float* dtc, int lim, int sl, int seqv) {
+                                                  const float* dtc, int lim, int sl, int seqv, int dcol, float dg) {
 #pragma unroll
   for (int i = 0; i < 32; i += 2) {
     float o[2];
@@ -664,58 +673,16 @@ __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t
         const int st = __shfl_sync(0xffffffffu, sl, i + j);   // all lanes shuffle, then combine
         ok = ok && (st == seqv);
       }
-      o[j] = v[i + j] * __expf(ok ? dA - dAc[i + j] : -INFINITY) * dtc[i + j];
+      o[j] = v[i + j] * __expf(ok ? dA - dAc[i + j] : -INFINITY) * dtc[i + j] + (i + j == dcol ? dg : 0.f);
     }
     pk[i / 2] = pack_bf16(o[0], o[1]);
   }
 }
 
-// SB, after its scores of chunk c: the skip term starts the Y accumulator, Y(c) = D x in f32
-// (row r = TMEM lane r), and MMA2(c) adds S x.  Y is free once the output of c-1 has read
-// it.  Then SB releases x(c) and signals Y_SEEDED.
-template <int NT>
-__device__ __forceinline__ bool seed_y(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tl, int c, int r) {
-  using G_ = Geo<NT>;
-  const int lane = r & 31;
-  const int xb = c % G_::XST, yb = c % G_::YB;
-  if (c >= G_::YB && !wait_bar(m, Y_FREE0 + yb, ((c / G_::YB) - 1) & 1, a.status)) return false;
-  ptx::tc_fence_after();   // order the TMEM stores after the wait that freed Y
-  if (a.D_ndim != 0) {
-    if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
-    const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
-#pragma unroll 1
-    for (int hx = 0; hx < 2; ++hx) {
-      float v[32];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint4 w = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, 4 * hx + k));
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = unpack_bf16(wv[j]);
-          v[8 * k + 2 * j] = m->Dv[32 * hx + 8 * k + 2 * j] * f.x;
-          v[8 * k + 2 * j + 1] = m->Dv[32 * hx + 8 * k + 2 * j + 1] * f.y;
-        }
-      }
-      ptx::tmem_st32(tl + COL_Y0 + 64 * yb + 32 * hx, v);
-    }
-    ptx::tmem_st_wait();
-  }
-  ptx::tc_fence_before();
-  __syncwarp();
-  if (lane == 0) {
-    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
-    ptx::mbar_arrive(&m->bar[Y_SEEDED0 + yb]);   // MMA2(c) may accumulate onto Y
-  }
-  TRACE(5, c, 4);
-  return true;
-}
-
 // ---------------------------------------------------------------------------
 // score workers SA (warps 4-7, half 0) and SB (warps 8-11, half 1).  Both build score
 // column blocks {half, half+2} of the rows of their quadrant (quadrant q has q+1 non-zero
-// blocks, so no warp does more than two).  SA also builds xs; SB first writes the output
-// of the previous chunk.
+// blocks, so no warp does more than two).  Each also builds half of xs first.
 // ---------------------------------------------------------------------------
 template <int NT, bool HAS_SEQ, bool HAS_Z>
 __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int half) {
@@ -724,6 +691,7 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const uint32_t tmem = m->tmem_base + ((uint32_t)(q * 32) << 16);
   constexpr bool has_seq = HAS_SEQ;
   const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
+  const float dg = m->Dh;
   using G_ = Geo<NT>;
   uint8_t* xs_sm = sm + G_::OFF_XS;
   const int nci = m->nci;
@@ -747,8 +715,9 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     const float dA = m->dA[buf][r];
     if (q == 0 || q == 3) TRACE(trole, c, 2);
 
-    if (half == 0) {
+    {
       // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
+      // SA writes head-dim columns 0-31, SB columns 32-63
       // exp(dA_last - dA_r) dt_r, from w_r = exp(dA_{32q} - dA_r) dt_r in a factored block
       const bool fq = block_factored(factor, m->dA[buf], q);
       const float e1 = __expf(m->dA[buf][QI - 1] - (fq ? m->dA[buf][32 * q] : dA)) * m->dt[buf][r];
@@ -758,7 +727,7 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       if (q == 0 || q == 3) TRACE(trole, c, 3);
       const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
+      for (int k = 4 * half; k < 4 * half + 4; ++k)
         *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, k)) =
             scale_row16(*reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, k)), scale);
       ptx::fence_proxy_async_smem();
@@ -795,8 +764,10 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         ptx::tmem_ld32(tS, v);   // one TMEM round trip per block
         ptx::tmem_ld_wait();
         if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
-        if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv);
-        else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv);
+        // the skip term D x rides on the diagonal: S[r][r] += D
+        const int dcol = k32 == q ? lane : -1;
+        if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv, dcol, dg);
+        else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         ptx::tmem_st16(tS, pk);
         if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
       }
@@ -818,7 +789,6 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     }
     if (q == 0 || q == 3) TRACE(trole, c, 7);
     if (q == 1 || q == 2) TRACE(7, c, 2 * half + (q == 2));
-    if (half == 1 && !seed_y<NT>(a, sm, m, tmem, c, r)) return;
   }
 }
 
@@ -827,7 +797,8 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
 // state worker T (warps 12-15).  S_{c+1} = decay_c S_c + B^T xs_c, with the product added
 // by MMA_L(c) onto the state T has already scaled in TMEM.  Per chunk c, once MMA_L(c) is
 // done: read S_{c+1}, write its bf16 copy for MMA3(c+1) (and the varlen / final state),
-// store decay_{c+1} S_{c+1} back for MMA_L(c+1), then seed Y(c).  Thread r owns state rows
+// store decay_{c+1} S_{c+1} back for MMA_L(c+1); the output epilogue of c-1 runs before
+// (one Yi buffer) or after (two) that copy.  Thread r owns state rows
 // n = r + 128*hh (TMEM lane r, 64 f32 columns per 128-row half).  decay_c is 0 when the
 // chunk-end sequence id changes (state_passing_fwd.py:208-225; the id before the first
 // chunk counts as 0).
@@ -903,8 +874,9 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     float* const vdst = sp.vslot >= 0 ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
     TRACE(5, c, 0);
     if (more && !chunk_decay<NT, HAS_SEQ>(a, m, bi, c + 1, r, prev_end, decay, sd_next)) return;
-    // MMA3(c) writes Yi after the output of c-1 has read it, so that output comes first
-    if (c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
+    // With one Yi buffer MMA3(c) writes Yi after the output of c-1 has read it, so that
+    // output comes first; with two it follows the state copy, overlapping MMA3/MMA_L(c+1).
+    if (G_::YIB == 1 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
     if (!wait_bar(m, B_L, c & 1, a.status)) return;   // S_{c+1} ready, MMA3(c) done with the copy of S_c
     TRACE(5, c, 1);
     ptx::tc_fence_after();
@@ -944,6 +916,7 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       }
     }
     TRACE(5, c, 2);
+    if (G_::YIB == 2 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
     sd_prev = sd_cur;
     sd_cur = sd_next;
   }
@@ -977,18 +950,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[X_EMPTY1], X_EMPTY_COUNT);
     ptx::mbar_init(&m->bar[CB_FREE0], 8);    // SA and SB done with the CB buffer
     ptx::mbar_init(&m->bar[CB_FREE1], 8);
-    ptx::mbar_init(&m->bar[XS_FULL], 4);
+    ptx::mbar_init(&m->bar[XS_FULL], 8);     // SA and SB: their halves of xs
     ptx::mbar_init(&m->bar[S_FULL_A0], 8);   // SA and SB: score blocks 0, 1
     ptx::mbar_init(&m->bar[S_FULL_A1], 8);
     ptx::mbar_init(&m->bar[S_FULL_B0], 8);   // SA and SB: score blocks 2, 3
     ptx::mbar_init(&m->bar[S_FULL_B1], 8);
-    ptx::mbar_init(&m->bar[Y_SEEDED0], 4);   // SB: Y seeded with D x
-    ptx::mbar_init(&m->bar[Y_SEEDED1], 4);
     ptx::mbar_init(&m->bar[ST_READY], 4);    // T: bf16 state copy for MMA3
     ptx::mbar_init(&m->bar[SCALED], 4);      // T: TMEM state scaled by the chunk decay
     ptx::mbar_init(&m->bar[Y_FREE0], 4);     // T: output read Y
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
-    ptx::mbar_init(&m->bar[YI_FREE], 4);     // T: output read Yi
+    ptx::mbar_init(&m->bar[YI_FREE0], 4);    // T: output read Yi
+    ptx::mbar_init(&m->bar[YI_FREE1], 4);
     ptx::mbar_init(&m->bar[DA_FREE0], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[DA_FREE1], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[STAGED], 4);
@@ -1006,7 +978,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   }
 #endif
   if (threadIdx.x < PT)
-    m->Dv[threadIdx.x] = a.D_ndim == 1 ? a.D[h] : a.D_ndim == 2 ? a.D[(int64_t)h * PT + threadIdx.x] : 0.f;
+    if (threadIdx.x == 0) m->Dh = a.D_ndim == 1 ? a.D[h] : 0.f;
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&a.tm_x);
     ptx::prefetch_tmap(&a.tm_b);
@@ -1189,6 +1161,8 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t L, uint6
 bool tc_supported(const ssd_fwd_params_t* p) {
   if (p->dtype != SSD_DTYPE_BF16 || p->headdim != PT || (p->dstate != 128 && p->dstate != 256)) return false;
   if (p->dA_cumsum || p->dt_out) return false;
+  // the skip term rides on the diagonal of the scores, which holds one D per head
+  if (p->D && p->D_ndim == 2) return false;
   // varlen states come from the per-sequence chunk schedule, which needs the seq_idx masks
   // inside the chunks it still shares with other sequences' rows.  With initial states the
   // reference's varlen result depends on its chunking (the first sequence sees the initial

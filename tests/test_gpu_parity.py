@@ -331,6 +331,27 @@ def test_tensor_core_path_selected():
             assert int(r.workspace[:4].view(torch.int32).item()) == 0  # device status word
 
 
+@pytest.mark.parametrize("Dshape", ["head", "head-dim"])
+def test_tensor_core_skip_term(Dshape):
+    """D per head rides on the diagonal of the bf16 scores in the fused kernel; D per
+    (head, head-dim column) cannot, and runs the stage pipeline.  Both within bf16 tolerance,
+    with |D| large enough that the skip term dominates the output."""
+    from mamba2_b200.runner import SsdForward
+    cfg = S.SsdConfig("t", 2, 384, 8, 64, 2, 128, 128, "bf16", has_z=True, has_init=True, return_final=True)
+    inp = S.make_ssd_inputs(cfg, 77)
+    rng = np.random.default_rng(3)
+    inp["D"] = (4.0 * rng.standard_normal((8,) if Dshape == "head" else (8, 64))).astype(np.float32)
+    d = dev_inputs(inp, "bf16")
+    r = SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], 128, D=d["D"], z=d["z"], dt_bias=d["dt_bias"],
+                   initial_states=d["initial_states"], dt_softplus=True, return_final_states=True)
+    assert r.uses_tc == (Dshape == "head")
+    out = r()
+    torch.cuda.synchronize()
+    ref_out, ref_final = _combined_oracle(inp, 128, cfg)[:2]
+    assert rel_l2(out, ref_out) <= TOL["bf16"]
+    assert rel_l2(r.final, ref_final) <= TOL["bf16"]
+
+
 @pytest.mark.parametrize("N,lens", [(256, None), (256, [100, 300, 7, 233]), (128, [128, 1, 300, 211])],
                          ids=["n256", "n256-seq", "n128-seq"])
 @pytest.mark.parametrize("z", [False, True])
