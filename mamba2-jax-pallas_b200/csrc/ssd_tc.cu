@@ -471,10 +471,11 @@ __device__ __forceinline__ int seq_at(const TcArgs& a, int bi, int64_t pos) {
 __device__ __forceinline__ uint4 scale_row16(uint4 w, float s) {
   uint4 o;
   float2 f;
-  f = unpack_bf16(w.x); o.x = pack_bf16(f.x * s, f.y * s);
-  f = unpack_bf16(w.y); o.y = pack_bf16(f.x * s, f.y * s);
-  f = unpack_bf16(w.z); o.z = pack_bf16(f.x * s, f.y * s);
-  f = unpack_bf16(w.w); o.w = pack_bf16(f.x * s, f.y * s);
+  const float2 ss = make_float2(s, s);
+  f = ptx::mul2(unpack_bf16(w.x), ss); o.x = pack_bf16(f.x, f.y);
+  f = ptx::mul2(unpack_bf16(w.y), ss); o.y = pack_bf16(f.x, f.y);
+  f = ptx::mul2(unpack_bf16(w.z), ss); o.z = pack_bf16(f.x, f.y);
+  f = ptx::mul2(unpack_bf16(w.w), ss); o.w = pack_bf16(f.x, f.y);
   return o;
 }
 
@@ -584,7 +585,11 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
     }
     ptx::tmem_ld_wait();
 #pragma unroll
-    for (int k = 0; k < 32; ++k) y[k] = fmaf(sdec, yi[k], y[k]);   // Y already holds D x (diagonal)
+    for (int k = 0; k < 32; k += 2) {   // Y already holds D x (diagonal)
+      const float2 o = ptx::fma2(make_float2(sdec, sdec), make_float2(yi[k], yi[k + 1]), make_float2(y[k], y[k + 1]));
+      y[k] = o.x;
+      y[k + 1] = o.y;
+    }
     if (HAS_Z) {
       if (out_x != nullptr && valid) {
 #pragma unroll
@@ -627,20 +632,35 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   return true;
 }
 
-// One 32-column block of scores for row r: v[i] holds CB[r][t] (t = 32*k32 + i) on entry.
-// FAC: t is below the quadrant's diagonal block, the decay is u_r * vl_t (vl in lane i);
-// otherwise exp(dA_r - dA_t) dt_t per element, masked to t <= r on the diagonal block.
 // One 32-column block of scores for row r (v holds CB[r][t], t = block start + i, on
 // entry; packed bf16 pairs on exit).  Factored blocks: decay u_r * w_t, w read from shared
-// memory (the same address in every lane).  Columns i > lim are masked (lim = lane on the
-// diagonal block, 31 below it).
-template <bool HAS_SEQ>
-__device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (&pk)[16], float u, const float* wc,
-                                                int lim, int sl, int seqv, int dcol, float dg) {
+// memory (the same address in every lane), two packed f32x2 products per column pair.
+
+// A block below the diagonal without sequence masks: every column counts.
+__device__ __forceinline__ void score_block_full(const float (&v)[32], uint32_t (&pk)[16], float u, const float* wc) {
+  const float2 uu = make_float2(u, u);
 #pragma unroll
   for (int i4 = 0; i4 < 8; ++i4) {
     const float4 w4 = *reinterpret_cast<const float4*>(wc + 4 * i4);
-    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+    const float2 p0 = ptx::mul2(make_float2(v[4 * i4], v[4 * i4 + 1]), ptx::mul2(uu, make_float2(w4.x, w4.y)));
+    const float2 p1 = ptx::mul2(make_float2(v[4 * i4 + 2], v[4 * i4 + 3]), ptx::mul2(uu, make_float2(w4.z, w4.w)));
+    pk[2 * i4] = pack_bf16(p0.x, p0.y);
+    pk[2 * i4 + 1] = pack_bf16(p1.x, p1.y);
+  }
+}
+
+// Masked: columns i > lim are zero (lim = lane on the diagonal block, 31 below it), and
+// with HAS_SEQ so are columns of another sequence; column dcol (the diagonal) adds dg.
+template <bool HAS_SEQ>
+__device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (&pk)[16], float u, const float* wc,
+                                                int lim, int sl, int seqv, int dcol, float dg) {
+  const float2 uu = make_float2(u, u);
+#pragma unroll
+  for (int i4 = 0; i4 < 8; ++i4) {
+    const float4 w4 = *reinterpret_cast<const float4*>(wc + 4 * i4);
+    const float2 p0 = ptx::mul2(make_float2(v[4 * i4], v[4 * i4 + 1]), ptx::mul2(uu, make_float2(w4.x, w4.y)));
+    const float2 p1 = ptx::mul2(make_float2(v[4 * i4 + 2], v[4 * i4 + 3]), ptx::mul2(uu, make_float2(w4.z, w4.w)));
+    const float pv[4] = {p0.x, p0.y, p1.x, p1.y};
     float o[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -651,7 +671,7 @@ __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (
         const int st = __shfl_sync(0xffffffffu, sl, i);
         ok = ok && (st == seqv);
       }
-      o[j] = (ok ? v[i] * (u * wv[j]) : 0.f) + (i == dcol ? dg : 0.f);
+      o[j] = (ok ? pv[j] : 0.f) + (i == dcol ? dg : 0.f);
     }
     pk[2 * i4] = pack_bf16(o[0], o[1]);
     pk[2 * i4 + 1] = pack_bf16(o[2], o[3]);
@@ -766,7 +786,8 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         if (q == 0 || q == 3) TRACE(trole, c, 11 + 2 * kk);
         // the skip term D x rides on the diagonal: S[r][r] += D
         const int dcol = k32 == q ? lane : -1;
-        if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv, dcol, dg);
+        if (fac && !HAS_SEQ && k32 < q) score_block_full(v, pk, __expf(dA - dAc[0]), wc);
+        else if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv, dcol, dg);
         else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         ptx::tmem_st16(tS, pk);
         if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
@@ -898,7 +919,11 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
               make_uint4(pack_bf16(sv[8 * j], sv[8 * j + 1]), pack_bf16(sv[8 * j + 2], sv[8 * j + 3]),
                          pack_bf16(sv[8 * j + 4], sv[8 * j + 5]), pack_bf16(sv[8 * j + 6], sv[8 * j + 7]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[i] *= decay;
+        for (int i = 0; i < 32; i += 2) {
+          const float2 d2 = ptx::mul2(make_float2(sv[i], sv[i + 1]), make_float2(decay, decay));
+          sv[i] = d2.x;
+          sv[i + 1] = d2.y;
+        }
         ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
       } else if (a.final_states) {
 #pragma unroll
