@@ -26,11 +26,11 @@
 // The only serial dependence between chunks is the state: E3(c) -> MMA3(c+1) -> E3(c+1).
 // Everything else is pipelined around it by warp role (16 warps, so every SM sub-partition
 // holds 4 warps and each thread may use 128 registers):
-//   warp 0      TMA producer (lane 0)
+//   warp 0      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
 //   warp 1      MMA issuer A (lane 0): MMA1, MMA2; owns the TMEM allocation (512 columns)
-//   warp 2      dA producer (lane 0): the chunk's cumulative dA and decay factors, computed
+//   warp 2      TMA producer (lane 0)
+//   warp 3      dA producer (lane 0): the chunk's cumulative dA and decay factors, computed
 //               by the dt pre-pass, bulk-copied into shared memory
-//   warp 3      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
 //   warps 4-7   SA: xs columns 0-31, score column blocks 0 and 2 of each row quadrant
 //   warps 8-11  SB: xs columns 32-63, score column blocks 1 and 3
 //   warps 12-15 T: the state recurrence E3 and the output epilogue E4 of the previous chunk
@@ -58,6 +58,11 @@ namespace {
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
 constexpr int NTHREADS = 512;
+// Single-lane roles of warps 0-3.  Warp w issues on SM sub-partition w % 4, which it shares
+// with the score and state warps of row quadrant w % 4; quadrant 3 has the most score work
+// (four 32-column blocks against one in quadrant 0), so the lightest role sits on 3 and
+// the state chain's MMA issuer on 0.
+constexpr int W_ISSUE_B = 0, W_ISSUE_A = 1, W_PRODUCER = 2, W_DA = 3;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MISC_BYTES = 2624;
 constexpr uint32_t SMEM_LAUNCH_BYTES = 232448;            // per-CTA maximum; the rest is alignment slack
@@ -233,7 +238,7 @@ __device__ __forceinline__ Span span_at(const TcArgs& a, int c) {
 }
 
 // ---------------------------------------------------------------------------
-// producer (warp 0, lane 0): per chunk, the C and B columns of the head's group in
+// producer (warp 2, lane 0): per chunk, the C and B columns of the head's group in
 // 128-column halves through a 2-stage ring, and the chunk's x tile through its own ring
 // ---------------------------------------------------------------------------
 template <int NT>
@@ -1002,9 +1007,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     a.trace[8 * 64 * 16 + 3 * blockIdx.x + 2] = smid;
   }
 #endif
-  if (threadIdx.x < PT)
-    if (threadIdx.x == 0) m->Dh = a.D_ndim == 1 ? a.D[h] : 0.f;
-  if (warp == 0 && lane == 0) {
+  if (threadIdx.x == 0) m->Dh = a.D_ndim == 1 ? a.D[h] : 0.f;
+  if (warp == W_PRODUCER && lane == 0) {
     ptx::prefetch_tmap(&a.tm_x);
     ptx::prefetch_tmap(&a.tm_b);
     ptx::prefetch_tmap(&a.tm_c);
@@ -1018,13 +1022,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   __syncthreads();
   ptx::tc_fence_after();
 
-  if (warp == 0) {
+  if (warp == W_PRODUCER) {
     if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
-  } else if (warp == 1) {
+  } else if (warp == W_ISSUE_A) {
     if (lane == 0) mma_issuer_a<NT>(a, sm, m);
-  } else if (warp == 2) {
+  } else if (warp == W_DA) {
     if (lane == 0) da_producer(a, m, bi, h);
-  } else if (warp == 3) {
+  } else if (warp == W_ISSUE_B) {
     if (lane == 0) mma_issuer_b<NT>(a, sm, m);
   } else if (warp < 12) {
     score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
