@@ -434,12 +434,76 @@ def run_ssu(args, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_conv(args, rank, world, device):
+    """conv: causal_conv1d of the c2 layer (nemotron-h-8b: dim = d_ssm + 2 G N = 10240,
+    L = 4096, width 4, bf16 weights and bias, SiLU) on the layer's channels-last
+    activations, 4 rotated input sets (each in + out 168 MB > L2)."""
+    from mamba2_b200 import causal_conv1d
+    hbm, _, peak_kind = _peaks()
+    b, L, dim, k = 1, 4096, 128 * 64 + 2 * 8 * 128, 4
+    for kv in args.override:
+        key, v = kv.split("=", 1)
+        if key in ("batch", "seqlen"):
+            b, L = (int(v), L) if key == "batch" else (b, int(v))
+    g = torch.Generator(device=device).manual_seed(2024 + rank)
+    sets = [torch.randn((b, L, dim), generator=g, device=device).to(torch.bfloat16) for _ in range(4)]
+    w = (0.5 * torch.randn((dim, k), generator=g, device=device)).to(torch.bfloat16)
+    bias = torch.randn((dim,), generator=g, device=device).to(torch.bfloat16)
+
+    def step(i):
+        return causal_conv1d(sets[i % 4].transpose(1, 2), w, bias=bias, activation="silu")
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    stream = torch.cuda.current_stream()
+    steps = args.steps
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(step, steps, stream)
+    clocks = clk.stop() if clk else None
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    kernel_ms = time_kernel(lambda: step(1))
+    byts = 2 * b * L * dim * 2
+    # e2e: pinned host activations in, the conv output back, both copies timed
+    host_in = sets[0].cpu().pin_memory()
+    host_out = torch.empty((b, L, dim), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(_i):
+        xd = host_in.to(device, non_blocking=True)
+        o = causal_conv1d(xd.transpose(1, 2), w, bias=bias, activation="silu")
+        host_out.copy_(o.transpose(1, 2), non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    ms_e2e = time_region(e2e_step, min(steps, 20), stream)
+    if rank != 0:
+        return
+    ach = byts / (kernel_ms / 1e3) / 1e9
+    line = {"metric": "causal_conv1d tokens/s", "value": steps * b * L * world / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "nemotron-h-8b conv1d (F1)", "key": "conv", "batch": b, "seqlen": L,
+                       "dim": dim, "width": k, "layout": "channels-last", "activation": "silu",
+                       "l2": "4 rotated input sets, each input + output > L2"},
+            "roofline": {"kernel": "conv1d_cl_kernel", "bound": "hbm", "achieved": ach, "peak": hbm,
+                         "unit": "GB/s", "frac": ach / hbm, "peak_kind": peak_kind,
+                         "traffic": measured_traffic("conv1d_cl_kernel/conv") if not args.override else None,
+                         "algorithmic_bytes": byts, "kernel_ms": kernel_ms},
+            "e2e": {"value": min(steps, 20) * b * L * world / (ms_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": host_in.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 2},
+            "gpu_launches": steps, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4", "conv"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--bf16-mma", action="store_true",
@@ -448,14 +512,14 @@ def main():
     ap.add_argument("--override", action="append", default=[],
                     help="key=value on the config (e.g. batch=32) for small profiling cases")
     args = ap.parse_args()
-    cfg = S.CONFIGS[args.config]
-    if args.override:
+    cfg = S.CONFIGS.get(args.config)
+    if args.override and cfg is not None:
         import dataclasses
         kv = dict(o.split("=", 1) for o in args.override)
         cfg = dataclasses.replace(cfg, **{k: type(getattr(cfg, k))(v) for k, v in kv.items()})
         S.CONFIGS[args.config] = cfg
-    if args.impl == "reference" and args.config == "c4":
-        raise SystemExit("reference arm for c4 not implemented")
+    if args.impl == "reference" and args.config in ("c4", "conv"):
+        raise SystemExit(f"reference arm for {args.config} not implemented")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
@@ -469,6 +533,8 @@ def main():
     try:
         if args.config == "c4":
             run_ssu(args, rank, world, device)
+        elif args.config == "conv":
+            run_conv(args, rank, world, device)
         else:
             run_ours(args, cfg, rank, world, device)
     finally:

@@ -210,6 +210,55 @@ typedef struct ssu_params {
  * instead of returned as a new array. */
 int ssd_selective_state_update(const ssu_params_t* p, ssd_stream_t stream);
 
+/* Causal depthwise conv1d over time (the step before the SSD in a Mamba2 layer).
+ * x and out are logically (batch, dim, seqlen), addressed by element strides, so the
+ * channels-last (batch, seqlen, dim) activations of the layer are read without a copy.
+ * out[b,d,t] = act(bias[d] + sum_j weight[d,j] * xm[b,d,t-(width-1)+j]) with xm = 0
+ * before t = 0, act = SiLU or identity.  With seq_idx, xm[b,d,t] = x[b,d,t] unless one of
+ * positions t+1 .. t+width-1 (inside the sequence) starts a new sequence id, in which case
+ * it is 0: the masking of causal_conv1d.py:143-193, which also drops those inputs from
+ * the outputs of their own sequence.  Arithmetic is f32; out is rounded once. */
+typedef struct ssd_conv1d_params {
+  int64_t batch, dim, seqlen;
+  int64_t x_stride_b, x_stride_d, x_stride_t;       /* element strides of x */
+  int64_t out_stride_b, out_stride_d, out_stride_t; /* element strides of out */
+  int32_t width;          /* kernel_size, 1 .. 8 */
+  int32_t dtype;          /* ssd_dtype_t of x */
+  int32_t out_dtype;      /* ssd_dtype_t of out */
+  int32_t silu;           /* nonzero: activation "silu" */
+  const void* x;
+  const float* weight;    /* (dim, width) f32, contiguous */
+  const float* bias;      /* (dim,) f32 or NULL */
+  const int32_t* seq_idx; /* (batch, seqlen) contiguous, or NULL */
+  void* out;              /* must not overlap x */
+} ssd_conv1d_params_t;
+
+/* Replaces causal_conv1d (src/mamba2_jax/ops/causal_conv1d.py:18-85). */
+int ssd_causal_conv1d_fwd(const ssd_conv1d_params_t* p, ssd_stream_t stream);
+
+/* One decode step of the conv: conv_state (batch, dim, width), width contiguous, is shifted
+ * left by one with x_new (batch, dim) written into its last slot, IN PLACE; then
+ * out[b,d] = act(bias[d] + sum_j weight[d,j] * conv_state[b,d,j]). */
+typedef struct ssd_conv1d_update_params {
+  int64_t batch, dim;
+  int64_t state_stride_b, state_stride_d;  /* element strides of conv_state (width: 1) */
+  int32_t width;          /* 1 .. 8 */
+  int32_t x_dtype;        /* ssd_dtype_t of x_new */
+  int32_t state_dtype;    /* ssd_dtype_t of conv_state */
+  int32_t out_dtype;      /* ssd_dtype_t of out */
+  int32_t silu;
+  int32_t reserved;
+  const void* x_new;      /* (batch, dim) contiguous */
+  void* conv_state;
+  const float* weight;    /* (dim, width) f32, contiguous */
+  const float* bias;      /* (dim,) f32 or NULL */
+  void* out;              /* (batch, dim) contiguous */
+} ssd_conv1d_update_params_t;
+
+/* Replaces causal_conv1d_update (src/mamba2_jax/ops/causal_conv1d.py:88-139); the state
+ * is updated in place instead of returned as a new array. */
+int ssd_causal_conv1d_update(const ssd_conv1d_update_params_t* p, ssd_stream_t stream);
+
 /* Thread-local description of the last failure on this host thread ("" if none). */
 const char* ssd_last_error(void);
 

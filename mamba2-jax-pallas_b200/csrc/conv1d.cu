@@ -1,0 +1,286 @@
+// Causal depthwise conv1d over time (causal_conv1d.py:18-85) and its decode step
+// (causal_conv1d.py:88-139).
+//
+//   xm[b,d,t]  = x[b,d,t] * keep[b,t]       keep = seq_idx constant on [t, t+width-1]
+//   out[b,d,t] = act(bias[d] + sum_j w[d,j] xm[b,d,t-(width-1)+j])   (xm = 0 before t = 0)
+//
+// keep restates _mask_sequence_boundaries (causal_conv1d.py:143-193): x[t] is zeroed when
+// any of positions t+1 .. t+width-1 (below seqlen) holds a different id than the position
+// before it, i.e. unless seq_idx is constant on [t, min(t+width-1, L-1)].
+//
+// Pure HBM stream: every input is read once and every output written once.  The layer's
+// activations are channels-last ((b, L, dim) with the conv over L), so the main kernel
+// walks a run of tokens per thread with 16 bytes of adjacent channels per load (coalesced
+// across the warp), keeps the last width-1 inputs in registers and has the run's keep mask
+// in shared memory.  Other layouts take a one-thread-per-output kernel.
+#include "common.cuh"
+#include "ssd_kernels.h"
+
+namespace ssd {
+
+namespace {
+
+constexpr int CL_THREADS = 128;
+constexpr int CL_RUN = 64;      // tokens per thread
+constexpr int CL_UNROLL = 4;    // tokens loaded ahead of use
+constexpr int GEN_THREADS = 256;
+constexpr int MAX_WIDTH = 8;
+
+struct ConvArgs {
+  int64_t dim, L;
+  int64_t xb, xd, xt, ob, od, ot;   // element strides
+  int width, silu;
+  const void* x;
+  const float* w;
+  const float* bias;
+  const int32_t* seq;
+  void* out;
+};
+
+__device__ __forceinline__ float act(float v, int silu_on) { return silu_on ? silu(v) : v; }
+
+// keep[t] for one batch row: seq constant on [t, min(t + width - 1, L - 1)]
+__device__ __forceinline__ float keep_at(const int32_t* seq_row, int64_t t, int64_t L, int width) {
+  if (seq_row == nullptr) return 1.f;
+  const int32_t s0 = seq_row[t];
+  for (int j = 1; j < width; ++j) {
+    if (t + j >= L) break;
+    if (seq_row[t + j] != s0) return 0.f;
+  }
+  return 1.f;
+}
+
+// V channels of one token as floats (16-byte load)
+template <typename T, int V>
+__device__ __forceinline__ void load_vec(const T* p, float (&v)[V]) {
+  const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(q.x); v[1] = __uint_as_float(q.y);
+    v[2] = __uint_as_float(q.z); v[3] = __uint_as_float(q.w);
+  } else {
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[2 * k] = __uint_as_float(u[k] << 16);
+      v[2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+    }
+  }
+}
+
+template <typename TO, int V>
+__device__ __forceinline__ void store_vec(TO* p, const float (&v)[V]) {
+  if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+    for (int k = 0; k < V; k += 4)
+      *reinterpret_cast<float4*>(p + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < V; k += 8) {
+      uint32_t u[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[k + 2 * i], v[k + 2 * i + 1]);
+        u[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(p + k) = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+  }
+}
+
+// Channels-last: x and out have unit channel stride.  Thread = V adjacent channels (16
+// bytes of x) over CL_RUN tokens; grid (channel blocks, token runs, batch).
+template <typename T, typename TO, int W>
+__global__ void __launch_bounds__(CL_THREADS) conv1d_cl_kernel(const ConvArgs a) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float keep[CL_RUN + W - 1];
+  const int64_t bi = blockIdx.z;
+  const int64_t t0 = (int64_t)blockIdx.y * CL_RUN;
+  const int64_t nt = min((int64_t)CL_RUN, a.L - t0);
+  const int32_t* seq_row = a.seq ? a.seq + bi * a.L : nullptr;
+  // keep for tokens t0-(W-1) .. t0+nt-1 (0 before the sequence start: causal zero padding)
+  for (int i = threadIdx.x; i < nt + W - 1; i += CL_THREADS) {
+    const int64_t t = t0 - (W - 1) + i;
+    keep[i] = t < 0 ? 0.f : keep_at(seq_row, t, a.L, W);
+  }
+  __syncthreads();
+  const int64_t c0 = ((int64_t)blockIdx.x * CL_THREADS + threadIdx.x) * V;
+  if (c0 >= a.dim) return;
+  const T* xp = (const T*)a.x + bi * a.xb + c0;
+  TO* op = (TO*)a.out + bi * a.ob + c0;
+  float w[V][W], bias[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) w[k][j] = __ldg(a.w + (c0 + k) * W + j);
+    bias[k] = a.bias ? __ldg(a.bias + c0 + k) : 0.f;
+  }
+  // window of the W-1 inputs before the current token, masked
+  float win[W > 1 ? W - 1 : 1][V];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) {
+    const int64_t t = t0 - (W - 1) + j;
+    const float kj = keep[j];
+    if (t >= 0) {
+      float v[V];
+      load_vec<T, V>(xp + t * a.xt, v);
+#pragma unroll
+      for (int k = 0; k < V; ++k) win[j][k] = v[k] * kj;
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) win[j][k] = 0.f;
+    }
+  }
+  for (int64_t i0 = 0; i0 < nt; i0 += CL_UNROLL) {
+    float xv[CL_UNROLL][V];
+#pragma unroll
+    for (int u = 0; u < CL_UNROLL; ++u) {
+      // unconditional clamped load (a conditional one would wait at its merge)
+      const int64_t t = t0 + min(i0 + u, nt - 1);
+      load_vec<T, V>(xp + t * a.xt, xv[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < CL_UNROLL; ++u) {
+      if (i0 + u >= nt) break;
+      const float kc = keep[i0 + u + W - 1];
+      float o[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float xc = xv[u][k] * kc;
+        float acc = bias[k];
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) acc = fmaf(w[k][j], win[j][k], acc);
+        acc = fmaf(w[k][W - 1], xc, acc);
+        o[k] = act(acc, a.silu);
+#pragma unroll
+        for (int j = 0; j + 1 < W - 1; ++j) win[j][k] = win[j + 1][k];
+        if (W > 1) win[W > 1 ? W - 2 : 0][k] = xc;
+      }
+      store_vec<TO, V>(op + (t0 + i0 + u) * a.ot, o);
+    }
+  }
+}
+
+// Any strides: one thread per output element.
+template <typename T, typename TO>
+__global__ void __launch_bounds__(GEN_THREADS) conv1d_generic_kernel(const ConvArgs a, int64_t total) {
+  const int64_t idx = (int64_t)blockIdx.x * GEN_THREADS + threadIdx.x;
+  if (idx >= total) return;
+  const int64_t t = idx % a.L, d = (idx / a.L) % a.dim, bi = idx / (a.L * a.dim);
+  const int32_t* seq_row = a.seq ? a.seq + bi * a.L : nullptr;
+  const T* xp = (const T*)a.x + bi * a.xb + d * a.xd;
+  float acc = a.bias ? a.bias[d] : 0.f;
+  for (int j = 0; j < a.width; ++j) {
+    const int64_t s = t - (a.width - 1) + j;
+    if (s < 0) continue;
+    acc = fmaf(a.w[d * a.width + j], ldg(xp + s * a.xt) * keep_at(seq_row, s, a.L, a.width), acc);
+  }
+  st((TO*)a.out + bi * a.ob + d * a.od + t * a.ot, act(acc, a.silu));
+}
+
+struct UpdArgs {
+  int64_t batch, dim, sb, sd;
+  int width, silu;
+  const void* x;
+  void* state;
+  const float* w;
+  const float* bias;
+  void* out;
+};
+
+template <typename TX, typename TS, typename TO>
+__global__ void __launch_bounds__(GEN_THREADS) conv1d_update_kernel(const UpdArgs a) {
+  const int64_t idx = (int64_t)blockIdx.x * GEN_THREADS + threadIdx.x;
+  if (idx >= a.batch * a.dim) return;
+  const int64_t bi = idx / a.dim, d = idx % a.dim;
+  TS* s = (TS*)a.state + bi * a.sb + d * a.sd;
+  float v[MAX_WIDTH];
+#pragma unroll
+  for (int j = 0; j < MAX_WIDTH; ++j)
+    if (j + 1 < a.width) v[j] = ld(s + j + 1);
+  {
+    // the new input as the state stores it (the output reads the stored values)
+    TS xs;
+    st(&xs, ldg((const TX*)a.x + idx));
+    v[a.width - 1 < MAX_WIDTH ? a.width - 1 : 0] = ld(&xs);
+  }
+  float acc = a.bias ? a.bias[d] : 0.f;
+#pragma unroll
+  for (int j = 0; j < MAX_WIDTH; ++j) {
+    if (j < a.width) {
+      st(s + j, v[j]);
+      acc = fmaf(a.w[d * a.width + j], v[j], acc);
+    }
+  }
+  st((TO*)a.out + idx, act(acc, a.silu));
+}
+
+template <typename T, typename TO>
+cudaError_t launch_cl(const ConvArgs& a, int64_t batch, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const dim3 grid((unsigned)((a.dim / V + CL_THREADS - 1) / CL_THREADS), (unsigned)((a.L + CL_RUN - 1) / CL_RUN),
+                  (unsigned)batch);
+  switch (a.width) {
+    case 1: conv1d_cl_kernel<T, TO, 1><<<grid, CL_THREADS, 0, st>>>(a); break;
+    case 2: conv1d_cl_kernel<T, TO, 2><<<grid, CL_THREADS, 0, st>>>(a); break;
+    case 3: conv1d_cl_kernel<T, TO, 3><<<grid, CL_THREADS, 0, st>>>(a); break;
+    case 4: conv1d_cl_kernel<T, TO, 4><<<grid, CL_THREADS, 0, st>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T, typename TO>
+cudaError_t launch_conv_typed(const ConvArgs& a, int64_t batch, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  // the vector store writes 16 bytes of bf16 at a time: f32 in, bf16 out is not vectorised
+  if constexpr (sizeof(TO) == 4 || V % 8 == 0) {
+    const bool cl = a.xd == 1 && a.od == 1 && a.width <= 4 && a.dim % V == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                    a.xb % V == 0 && a.xt % V == 0 && a.ob % V == 0 && a.ot % V == 0;
+    if (cl) return launch_cl<T, TO>(a, batch, st);
+  }
+  const int64_t total = batch * a.dim * a.L;
+  conv1d_generic_kernel<T, TO><<<(unsigned)((total + GEN_THREADS - 1) / GEN_THREADS), GEN_THREADS, 0, st>>>(a, total);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// The channels-last kernel takes widths 1-4 (Mamba2's d_conv is 4); wider kernels, odd
+// strides and unaligned pointers run the one-thread-per-output kernel.
+cudaError_t launch_conv1d(const ssd_conv1d_params_t* p, cudaStream_t st) {
+  ConvArgs a;
+  a.dim = p->dim; a.L = p->seqlen;
+  a.xb = p->x_stride_b; a.xd = p->x_stride_d; a.xt = p->x_stride_t;
+  a.ob = p->out_stride_b; a.od = p->out_stride_d; a.ot = p->out_stride_t;
+  a.width = p->width; a.silu = p->silu != 0;
+  a.x = p->x; a.w = p->weight; a.bias = p->bias; a.seq = p->seq_idx; a.out = p->out;
+  const bool xf = p->dtype == SSD_DTYPE_F32, of = p->out_dtype == SSD_DTYPE_F32;
+  if (xf && of) return launch_conv_typed<float, float>(a, p->batch, st);
+  if (xf) return launch_conv_typed<float, bf16>(a, p->batch, st);
+  if (of) return launch_conv_typed<bf16, float>(a, p->batch, st);
+  return launch_conv_typed<bf16, bf16>(a, p->batch, st);
+}
+
+cudaError_t launch_conv1d_update(const ssd_conv1d_update_params_t* p, cudaStream_t st) {
+  UpdArgs a;
+  a.batch = p->batch; a.dim = p->dim; a.sb = p->state_stride_b; a.sd = p->state_stride_d;
+  a.width = p->width; a.silu = p->silu != 0;
+  a.x = p->x_new; a.state = p->conv_state; a.w = p->weight; a.bias = p->bias; a.out = p->out;
+  const unsigned grid = (unsigned)((p->batch * p->dim + GEN_THREADS - 1) / GEN_THREADS);
+  const int code = (p->x_dtype == SSD_DTYPE_F32 ? 4 : 0) + (p->state_dtype == SSD_DTYPE_F32 ? 2 : 0) +
+                   (p->out_dtype == SSD_DTYPE_F32 ? 1 : 0);
+  switch (code) {
+    case 0: conv1d_update_kernel<bf16, bf16, bf16><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 1: conv1d_update_kernel<bf16, bf16, float><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 2: conv1d_update_kernel<bf16, float, bf16><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 3: conv1d_update_kernel<bf16, float, float><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 4: conv1d_update_kernel<float, bf16, bf16><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 5: conv1d_update_kernel<float, bf16, float><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    case 6: conv1d_update_kernel<float, float, bf16><<<grid, GEN_THREADS, 0, st>>>(a); break;
+    default: conv1d_update_kernel<float, float, float><<<grid, GEN_THREADS, 0, st>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ssd

@@ -32,6 +32,8 @@ cudaError_t launch_chunk_state_varlen(const void* B, const void* x, int dtype, c
                                       int states_dtype, int64_t T_total, int64_t H, int64_t P,
                                       int64_t G, int64_t N, int64_t Q, float* out, cudaStream_t st);
 cudaError_t launch_ssu(const ssu_params_t* p, cudaStream_t st);
+cudaError_t launch_conv1d(const ssd_conv1d_params_t* p, cudaStream_t st);
+cudaError_t launch_conv1d_update(const ssd_conv1d_update_params_t* p, cudaStream_t st);
 
 // Set the thread-local message ssd_last_error() returns.
 void set_last_error(const char* msg);

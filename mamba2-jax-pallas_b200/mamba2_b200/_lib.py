@@ -33,7 +33,7 @@ EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
             "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_combined_fwd_noalloc", "ssd_chunk_cumsum_fwd",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
-            "ssd_last_error", "ssd_abi_version"]
+            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_last_error", "ssd_abi_version"]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -60,6 +60,21 @@ class SsuParams(ctypes.Structure):
                 ("dt_softplus", _i32), ("reserved", _i32),
                 ("state", _vp), ("x", _vp), ("dt", _vp), ("A", _vp), ("B", _vp), ("C", _vp),
                 ("D", _vp), ("z", _vp), ("dt_bias", _vp), ("out", _vp)]
+
+
+class Conv1dParams(ctypes.Structure):
+    _fields_ = [("batch", _i64), ("dim", _i64), ("seqlen", _i64),
+                ("x_stride_b", _i64), ("x_stride_d", _i64), ("x_stride_t", _i64),
+                ("out_stride_b", _i64), ("out_stride_d", _i64), ("out_stride_t", _i64),
+                ("width", _i32), ("dtype", _i32), ("out_dtype", _i32), ("silu", _i32),
+                ("x", _vp), ("weight", _vp), ("bias", _vp), ("seq_idx", _vp), ("out", _vp)]
+
+
+class Conv1dUpdateParams(ctypes.Structure):
+    _fields_ = [("batch", _i64), ("dim", _i64), ("state_stride_b", _i64), ("state_stride_d", _i64),
+                ("width", _i32), ("x_dtype", _i32), ("state_dtype", _i32), ("out_dtype", _i32),
+                ("silu", _i32), ("reserved", _i32),
+                ("x_new", _vp), ("conv_state", _vp), ("weight", _vp), ("bias", _vp), ("out", _vp)]
 
 
 class SsdError(RuntimeError):
@@ -102,6 +117,8 @@ def load() -> ctypes.CDLL:
     lib.ssd_chunk_scan_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp,
                                        _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
                                        _vp]
+    lib.ssd_causal_conv1d_fwd.argtypes = [P(Conv1dParams), _vp]
+    lib.ssd_causal_conv1d_update.argtypes = [P(Conv1dUpdateParams), _vp]
     lib.ssd_chunk_state_varlen_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _i32,
                                                _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
     lib.ssd_selective_state_update.argtypes = [P(SsuParams), _vp]

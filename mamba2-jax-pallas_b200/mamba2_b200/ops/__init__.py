@@ -1,4 +1,5 @@
-"""Decode-step op (B200 replacement of ``src/mamba2_jax/ops/selective_state_update.py``)."""
+"""Ops around the SSD (B200 replacements of ``src/mamba2_jax/ops``)."""
+from .causal_conv1d import causal_conv1d, causal_conv1d_update
 from .selective_state_update import selective_state_update
 
-__all__ = ["selective_state_update"]
+__all__ = ["selective_state_update", "causal_conv1d", "causal_conv1d_update"]

@@ -382,6 +382,64 @@ def selective_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
 
 
 # ---------------------------------------------------------------------------
+# F1  causal_conv1d (the step before the SSD)
+# ---------------------------------------------------------------------------
+
+def conv1d_keep(seq_idx, width):
+    """``causal_conv1d.py:143-193`` (_mask_sequence_boundaries): the (b, L) 0/1 factor on x.
+
+    boundary[t] = t == 0 or seq[t] != seq[t-1]; for each lag j in 1..width-1, x[t] is
+    zeroed when boundary[t+j] (positions past the end count as no boundary).
+    """
+    seq = np.asarray(seq_idx)
+    b, L = seq.shape
+    boundary = np.concatenate([np.ones((b, 1), bool), seq[:, 1:] != seq[:, :-1]], axis=1)
+    keep = np.ones((b, L), F64)
+    for j in range(1, width):
+        shifted = np.concatenate([boundary[:, j:], np.zeros((b, min(j, L)), bool)], axis=1)[:, :L]
+        keep = keep * (1.0 - shifted)
+    return keep
+
+
+def causal_conv1d(x, weight, bias=None, activation=None, seq_idx=None):
+    """``causal_conv1d.py:18-85``: x (b, d, L), weight (d, k) or (d, 1, k) -> (b, d, L).
+
+    lax.conv_general_dilated is a cross-correlation over the left-padded input, so
+    out[t] = sum_j w[j] x[t - (k-1) + j]: w[k-1] multiplies the newest input.
+    """
+    x, w = _f(x), _f(weight)
+    if w.ndim == 3:
+        w = w[:, 0, :]
+    b, d, L = x.shape
+    k = w.shape[1]
+    if seq_idx is not None:
+        x = x * conv1d_keep(seq_idx, k)[:, None, :]
+    xp = np.concatenate([np.zeros((b, d, k - 1)), x], axis=2)
+    out = np.zeros((b, d, L))
+    for j in range(k):
+        out += w[None, :, j:j + 1] * xp[:, :, j:j + L]
+    if bias is not None:
+        out = out + _f(bias)[None, :, None]
+    if activation == "silu":
+        out = silu(out)
+    return out
+
+
+def causal_conv1d_update(x_new, conv_state, weight, bias=None, activation=None):
+    """``causal_conv1d.py:88-139``: returns (new_conv_state, out)."""
+    s, w = _f(conv_state), _f(weight)
+    if w.ndim == 3:
+        w = w[:, 0, :]
+    new = np.concatenate([s[:, :, 1:], _f(x_new)[:, :, None]], axis=-1)
+    out = np.sum(new * w[None], axis=-1)
+    if bias is not None:
+        out = out + _f(bias)[None]
+    if activation == "silu":
+        out = silu(out)
+    return new, out
+
+
+# ---------------------------------------------------------------------------
 # helpers
 # ---------------------------------------------------------------------------
 
