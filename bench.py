@@ -498,12 +498,76 @@ def run_conv(args, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_norm(args, rank, world, device):
+    """norm: rms_norm_gated of the c2 layer (nemotron-h-8b: the SSD output y (1, 4096, 8192)
+    f32, gate z bf16, weight f32, group = d_ssm / G = 1024, norm before gate), 4 rotated
+    input sets (each y + z + out 335 MB > L2)."""
+    from mamba2_b200 import rms_norm_gated
+    hbm, _, peak_kind = _peaks()
+    b, L, d, G = 1, 4096, 128 * 64, 8
+    for kv in args.override:
+        key, v = kv.split("=", 1)
+        if key in ("batch", "seqlen"):
+            b, L = (int(v), L) if key == "batch" else (b, int(v))
+    g = torch.Generator(device=device).manual_seed(4048 + rank)
+    ys = [torch.randn((b, L, d), generator=g, device=device) for _ in range(4)]
+    zs = [torch.randn((b, L, d), generator=g, device=device).to(torch.bfloat16) for _ in range(4)]
+    w = 1.0 + 0.1 * torch.randn((d,), generator=g, device=device)
+
+    def step(i):
+        return rms_norm_gated(ys[i % 4], w, z=zs[i % 4], group_size=d // G)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    stream = torch.cuda.current_stream()
+    steps = args.steps
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(step, steps, stream)
+    clocks = clk.stop() if clk else None
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    kernel_ms = time_kernel(lambda: step(1))
+    byts = b * L * d * (4 + 2 + 4) + d * 4
+    host_y, host_z = ys[0].cpu().pin_memory(), zs[0].cpu().pin_memory()
+    host_out = torch.empty((b, L, d)).pin_memory()
+
+    def e2e_step(_i):
+        o = rms_norm_gated(host_y.to(device, non_blocking=True), w,
+                           z=host_z.to(device, non_blocking=True), group_size=d // G)
+        host_out.copy_(o, non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    ms_e2e = time_region(e2e_step, min(steps, 20), stream)
+    if rank != 0:
+        return
+    ach = byts / (kernel_ms / 1e3) / 1e9
+    line = {"metric": "rms_norm_gated tokens/s", "value": steps * b * L * world / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "nemotron-h-8b gated RMSNorm (F2)", "key": "norm", "batch": b, "seqlen": L,
+                       "hidden": d, "group_size": d // G, "y": "f32", "z": "bf16", "norm_before_gate": True,
+                       "l2": "4 rotated input sets, each y + z + out > L2"},
+            "roofline": {"kernel": "rmsnorm_cached_kernel", "bound": "hbm", "achieved": ach, "peak": hbm,
+                         "unit": "GB/s", "frac": ach / hbm, "peak_kind": peak_kind,
+                         "traffic": measured_traffic("rmsnorm_cached_kernel/norm") if not args.override else None,
+                         "algorithmic_bytes": byts, "kernel_ms": kernel_ms},
+            "e2e": {"value": min(steps, 20) * b * L * world / (ms_e2e / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": host_y.numel() * 4 + host_z.numel() * 2,
+                    "d2h_bytes_per_step": host_out.numel() * 4},
+            "gpu_launches": steps, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4", "conv"])
+    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4", "conv", "norm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--bf16-mma", action="store_true",
@@ -518,7 +582,7 @@ def main():
         kv = dict(o.split("=", 1) for o in args.override)
         cfg = dataclasses.replace(cfg, **{k: type(getattr(cfg, k))(v) for k, v in kv.items()})
         S.CONFIGS[args.config] = cfg
-    if args.impl == "reference" and args.config in ("c4", "conv"):
+    if args.impl == "reference" and args.config in ("c4", "conv", "norm"):
         raise SystemExit(f"reference arm for {args.config} not implemented")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -535,6 +599,8 @@ def main():
             run_ssu(args, rank, world, device)
         elif args.config == "conv":
             run_conv(args, rank, world, device)
+        elif args.config == "norm":
+            run_norm(args, rank, world, device)
         else:
             run_ours(args, cfg, rank, world, device)
     finally:

@@ -259,6 +259,29 @@ typedef struct ssd_conv1d_update_params {
  * is updated in place instead of returned as a new array. */
 int ssd_causal_conv1d_update(const ssd_conv1d_update_params_t* p, ssd_stream_t stream);
 
+/* Gated RMSNorm over groups of the last axis (the step after the SSD in a Mamba2 layer).
+ * x, z and out are logically (rows, hidden): the last axis is contiguous, rows are addressed
+ * by an element stride.  For each row and each group of group_size values (hidden must be a
+ * multiple of group_size):
+ *   norm_before_gate != 0:  out = x / sqrt(mean(x^2) + eps) * weight * silu(z)
+ *   norm_before_gate == 0:  v = x * silu(z); out = v / sqrt(mean(v^2) + eps) * weight
+ * z may be NULL (no gate).  Arithmetic is f32 (IEEE sqrt and division); out is rounded once. */
+typedef struct ssd_rms_norm_params {
+  int64_t rows, hidden, group_size;
+  int64_t x_stride_row, z_stride_row, out_stride_row;  /* element strides between rows */
+  int32_t x_dtype, z_dtype, weight_dtype, out_dtype;   /* ssd_dtype_t each */
+  int32_t norm_before_gate;
+  float eps;
+  const void* x;
+  const void* z;          /* or NULL */
+  const void* weight;     /* (hidden,) contiguous */
+  void* out;              /* must not partially overlap x or z (out == x is allowed) */
+} ssd_rms_norm_params_t;
+
+/* Replaces rms_norm_gated (src/mamba2_jax/ops/rms_norm.py:15-92), called by the Mamba2
+ * mixer at src/mamba2_jax/modules/mamba2.py:401-406 with group_size = d_ssm / ngroups. */
+int ssd_rms_norm_gated(const ssd_rms_norm_params_t* p, ssd_stream_t stream);
+
 /* Thread-local description of the last failure on this host thread ("" if none). */
 const char* ssd_last_error(void);
 

@@ -384,4 +384,19 @@ int ssd_causal_conv1d_update(const ssd_conv1d_update_params_t* p, ssd_stream_t s
   return cuda_status(ssd::launch_conv1d_update(p, (cudaStream_t)stream), "causal_conv1d_update");
 }
 
+int ssd_rms_norm_gated(const ssd_rms_norm_params_t* p, ssd_stream_t stream) {
+  g_err[0] = 0;
+  if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
+  if (p->rows <= 0 || p->hidden <= 0 || p->group_size <= 0) return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
+  if (p->hidden % p->group_size != 0) return fail(SSD_ERR_INVALID_ARG, "hidden must be a multiple of group_size");
+  if (!dtype_ok(p->x_dtype) || !dtype_ok(p->weight_dtype) || !dtype_ok(p->out_dtype) ||
+      (p->z && !dtype_ok(p->z_dtype)))
+    return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (!p->x || !p->weight || !p->out) return fail(SSD_ERR_INVALID_ARG, "x, weight and out are required");
+  if (p->x_stride_row < p->hidden || p->out_stride_row < p->hidden || (p->z && p->z_stride_row < p->hidden))
+    return fail(SSD_ERR_INVALID_ARG, "row strides must be at least hidden");
+  if (!(p->eps >= 0.f)) return fail(SSD_ERR_INVALID_ARG, "eps must be non-negative");
+  return cuda_status(ssd::launch_rms_norm_gated(p, (cudaStream_t)stream), "rms_norm_gated");
+}
+
 }  // extern "C"

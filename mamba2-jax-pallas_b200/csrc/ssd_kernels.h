@@ -34,6 +34,7 @@ cudaError_t launch_chunk_state_varlen(const void* B, const void* x, int dtype, c
 cudaError_t launch_ssu(const ssu_params_t* p, cudaStream_t st);
 cudaError_t launch_conv1d(const ssd_conv1d_params_t* p, cudaStream_t st);
 cudaError_t launch_conv1d_update(const ssd_conv1d_update_params_t* p, cudaStream_t st);
+cudaError_t launch_rms_norm_gated(const ssd_rms_norm_params_t* p, cudaStream_t st);
 
 // Set the thread-local message ssd_last_error() returns.
 void set_last_error(const char* msg);

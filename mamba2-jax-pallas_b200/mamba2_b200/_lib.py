@@ -33,7 +33,7 @@ EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
             "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_combined_fwd_noalloc", "ssd_chunk_cumsum_fwd",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
-            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_last_error", "ssd_abi_version"]
+            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_last_error", "ssd_abi_version"]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -75,6 +75,14 @@ class Conv1dUpdateParams(ctypes.Structure):
                 ("width", _i32), ("x_dtype", _i32), ("state_dtype", _i32), ("out_dtype", _i32),
                 ("silu", _i32), ("reserved", _i32),
                 ("x_new", _vp), ("conv_state", _vp), ("weight", _vp), ("bias", _vp), ("out", _vp)]
+
+
+class RmsNormParams(ctypes.Structure):
+    _fields_ = [("rows", _i64), ("hidden", _i64), ("group_size", _i64),
+                ("x_stride_row", _i64), ("z_stride_row", _i64), ("out_stride_row", _i64),
+                ("x_dtype", _i32), ("z_dtype", _i32), ("weight_dtype", _i32), ("out_dtype", _i32),
+                ("norm_before_gate", _i32), ("eps", _f32),
+                ("x", _vp), ("z", _vp), ("weight", _vp), ("out", _vp)]
 
 
 class SsdError(RuntimeError):
@@ -119,6 +127,7 @@ def load() -> ctypes.CDLL:
                                        _vp]
     lib.ssd_causal_conv1d_fwd.argtypes = [P(Conv1dParams), _vp]
     lib.ssd_causal_conv1d_update.argtypes = [P(Conv1dUpdateParams), _vp]
+    lib.ssd_rms_norm_gated.argtypes = [P(RmsNormParams), _vp]
     lib.ssd_chunk_state_varlen_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _i32,
                                                _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
     lib.ssd_selective_state_update.argtypes = [P(SsuParams), _vp]

@@ -440,6 +440,30 @@ def causal_conv1d_update(x_new, conv_state, weight, bias=None, activation=None):
 
 
 # ---------------------------------------------------------------------------
+# F2  rms_norm_gated (the step after the SSD)
+# ---------------------------------------------------------------------------
+
+def rms_norm_gated(x, weight, z=None, eps=1e-5, group_size=None, norm_before_gate=True):
+    """``ops/rms_norm.py:15-92``: RMS over groups of ``group_size`` of the last axis.
+
+    norm_before_gate: out = x / sqrt(mean_g(x^2) + eps) * weight * silu(z); otherwise x is
+    multiplied by silu(z) first and the gate is not applied again (``:57-66``, ``:76-91``).
+    """
+    x, w = _f(x), _f(weight)
+    hidden = x.shape[-1]
+    gs = hidden if group_size is None else int(group_size)
+    assert hidden % gs == 0
+    if z is not None and not norm_before_gate:
+        x = x * silu(_f(z))
+    xg = x.reshape(*x.shape[:-1], hidden // gs, gs)
+    rms = np.sqrt(np.mean(xg * xg, axis=-1, keepdims=True) + eps)
+    out = (xg / rms).reshape(x.shape) * w
+    if z is not None and norm_before_gate:
+        out = out * silu(_f(z))
+    return out
+
+
+# ---------------------------------------------------------------------------
 # helpers
 # ---------------------------------------------------------------------------
 
