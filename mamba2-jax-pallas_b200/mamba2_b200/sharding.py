@@ -14,7 +14,8 @@ combine (a1, s1) o (a2, s2) = (a1 a2, a2 s1 + s2) is associative, so each rank n
 exclusive prefix of the pairs of the ranks before it.  That prefix is exchanged by
 recursive doubling with point-to-point sends (log2(world) rounds of (b,H) + (b,H,P,N)
 fp32 per rank), then every rank reruns its segment with the received state as its
-initial state.  The exchange is the only collective of the path.
+initial state; with packed sequences only the chunks that hold the carried sequence are
+rerun.  The exchange is the only collective of the path.
 """
 from __future__ import annotations
 
@@ -193,5 +194,30 @@ def ssd_forward_sequence_parallel(x, dt, A, B, C, chunk_size, D=None, z=None, dt
     if rank == 0:
         return out0, s_loc   # pass 1 already started from the sequence's initial state
     # pass 2: the segment with the received state (applies to the carried sequence, id 0)
-    return mamba_chunk_scan_combined_fwd(x, dt, A, B, C, chunk_size, initial_states=s_in.contiguous(), seq_idx=sq,
-                                         return_final_states=True, **kw)
+    lp = carried_prefix(sq, chunk_size) if sq is not None else L
+    if lp == 0:
+        return out0, s_loc   # the segment starts a new sequence: the state does not enter
+    if lp >= L:
+        return mamba_chunk_scan_combined_fwd(x, dt, A, B, C, chunk_size, initial_states=s_in.contiguous(),
+                                             seq_idx=sq, return_final_states=True, **kw)
+    # The carried sequence ends inside the first lp tokens of every batch row: only those
+    # chunks see the received state.  The later tokens and the final state (which decays
+    # through a sequence reset to exactly 0 before them) are pass 1's.
+    sl = lambda t: None if t is None else t[:, :lp]
+    kw2 = dict(kw, z=sl(z))
+    out_p, _ = mamba_chunk_scan_combined_fwd(sl(x), sl(dt), A, sl(B), sl(C), chunk_size,
+                                             initial_states=s_in.contiguous(), seq_idx=sl(sq),
+                                             return_final_states=True, **kw2)
+    out0[:, :lp] = out_p
+    return out0, s_loc
+
+
+def carried_prefix(seq_idx: torch.Tensor, chunk_size: int) -> int:
+    """Tokens of a segment, rounded up to whole chunks, that hold the carried sequence (id 0
+    after relabel_seq_idx) in every batch row: the first position with another id, maxed
+    over rows (the segment length if some row never leaves it)."""
+    b, L = seq_idx.shape
+    other = seq_idx != 0
+    first = torch.where(other.any(1), other.int().argmax(1), torch.full((b,), L, device=seq_idx.device))
+    t_end = int(first.max().item())
+    return min(L, -(-t_end // chunk_size) * chunk_size)

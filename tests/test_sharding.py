@@ -136,7 +136,7 @@ def _oracle(inp, Q, init, seq):
                           return_final_states=True)
 
 
-@pytest.mark.parametrize("lens", [None, [100, 230, 60, 250]], ids=["one-seq", "packed"])
+@pytest.mark.parametrize("lens", [None, [100, 230, 60, 250], [320, 320]], ids=["one-seq", "packed", "cut-at-segment"])
 @pytest.mark.parametrize("world", [2, 3])
 def test_sequence_parallel_algorithm_matches_oracle(world, lens):
     L, Q = 640, 64
@@ -163,7 +163,14 @@ def test_sequence_parallel_algorithm_matches_oracle(world, lens):
             outs.append(out_loc)
             a = np.zeros_like(a)
         else:
-            outs.append(_oracle(sin, Q, acc_s, sq)[0])      # rerun with the received state
+            # rerun with the received state, only over the chunks holding the carried sequence
+            lp = L if sq is None else SH.carried_prefix(torch.from_numpy(sq), Q)
+            o2 = out_loc.copy()
+            if lp > 0:
+                pre = {k: (v[:, :lp] if k in ("x", "dt", "B", "C", "z") and v is not None else v)
+                       for k, v in sin.items()}
+                o2[:, :lp] = _oracle(pre, Q, acc_s, None if sq is None else sq[:, :lp])[0]
+            outs.append(o2)
         acc_a, acc_s = acc_a * a, a[..., None, None] * acc_s + s_loc
     np.testing.assert_allclose(np.concatenate(outs, 1), full_out, rtol=1e-9, atol=1e-9)
     np.testing.assert_allclose(acc_s, full_final, rtol=1e-9, atol=1e-9)
@@ -197,7 +204,8 @@ def _sp_gpu_worker(rank, world, port, q, lens):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("lens", [None, [300, 500, 224]], ids=["one-seq", "packed"])
+@pytest.mark.parametrize("lens", [None, [300, 500, 224], [300, 212, 512]],
+                         ids=["one-seq", "packed", "new-seq-at-segment"])
 def test_sequence_parallel_forward_two_ranks_one_gpu(lens):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -205,6 +213,14 @@ def test_sequence_parallel_forward_two_ranks_one_gpu(lens):
     for r in range(2):
         assert res[r][0] <= 1e-2, (r, res[r])
         assert res[r][1] <= 1e-2, (r, res[r])
+
+
+def test_carried_prefix():
+    sq = torch.tensor([[0, 0, 0, 1, 1, 2, 2, 2], [0, 0, 0, 0, 0, 1, 1, 1]], dtype=torch.int32)
+    assert SH.carried_prefix(sq, 2) == 6       # row 1 leaves at 5 -> 3 chunks
+    assert SH.carried_prefix(sq[:1], 4) == 4
+    assert SH.carried_prefix(torch.zeros((1, 8), dtype=torch.int32), 4) == 8
+    assert SH.carried_prefix(torch.ones((1, 8), dtype=torch.int32), 4) == 0
 
 
 @pytest.mark.gpu
