@@ -21,8 +21,7 @@ namespace ssd {
 namespace {
 
 constexpr int CL_THREADS = 128;
-constexpr int CL_RUN = 64;      // tokens per thread
-constexpr int CL_UNROLL = 4;    // tokens loaded ahead of use
+constexpr int CL_RUN = 16;      // tokens per thread, all loaded up front
 constexpr int GEN_THREADS = 256;
 constexpr int MAX_WIDTH = 8;
 
@@ -50,23 +49,6 @@ __device__ __forceinline__ float keep_at(const int32_t* seq_row, int64_t t, int6
   return 1.f;
 }
 
-// V channels of one token as floats (16-byte load)
-template <typename T, int V>
-__device__ __forceinline__ void load_vec(const T* p, float (&v)[V]) {
-  const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
-  if constexpr (sizeof(T) == 4) {
-    v[0] = __uint_as_float(q.x); v[1] = __uint_as_float(q.y);
-    v[2] = __uint_as_float(q.z); v[3] = __uint_as_float(q.w);
-  } else {
-    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[2 * k] = __uint_as_float(u[k] << 16);
-      v[2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
-    }
-  }
-}
-
 template <typename TO, int V>
 __device__ __forceinline__ void store_vec(TO* p, const float (&v)[V]) {
   if constexpr (sizeof(TO) == 4) {
@@ -87,76 +69,89 @@ __device__ __forceinline__ void store_vec(TO* p, const float (&v)[V]) {
   }
 }
 
+// 16 bytes of x as V floats
+template <typename T, int V>
+__device__ __forceinline__ void unpack_vec(const uint4 q, float (&v)[V]) {
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(q.x); v[1] = __uint_as_float(q.y);
+    v[2] = __uint_as_float(q.z); v[3] = __uint_as_float(q.w);
+  } else {
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[2 * k] = __uint_as_float(u[k] << 16);
+      v[2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+    }
+  }
+}
+
 // Channels-last: x and out have unit channel stride.  Thread = V adjacent channels (16
-// bytes of x) over CL_RUN tokens; grid (channel blocks, token runs, batch).
+// bytes of x) over CL_RUN tokens; grid (channel blocks, token runs, batch).  Every load of
+// the run (CL_RUN + W - 1 tokens of 16 bytes) is issued before the first output is
+// computed, so a thread has ~300 bytes in flight; the runs are short so that the grid is
+// several waves deep (the c2 layer: 2560 blocks) and its last wave is a small share.
 template <typename T, typename TO, int W>
 __global__ void __launch_bounds__(CL_THREADS) conv1d_cl_kernel(const ConvArgs a) {
   constexpr int V = 16 / sizeof(T);
-  __shared__ float keep[CL_RUN + W - 1];
+  constexpr int NL = CL_RUN + W - 1;
+  __shared__ float keep[NL];
   const int64_t bi = blockIdx.z;
   const int64_t t0 = (int64_t)blockIdx.y * CL_RUN;
   const int64_t nt = min((int64_t)CL_RUN, a.L - t0);
   const int32_t* seq_row = a.seq ? a.seq + bi * a.L : nullptr;
   // keep for tokens t0-(W-1) .. t0+nt-1 (0 before the sequence start: causal zero padding)
-  for (int i = threadIdx.x; i < nt + W - 1; i += CL_THREADS) {
+  for (int i = threadIdx.x; i < NL; i += CL_THREADS) {
     const int64_t t = t0 - (W - 1) + i;
-    keep[i] = t < 0 ? 0.f : keep_at(seq_row, t, a.L, W);
+    keep[i] = (t < 0 || i >= nt + W - 1) ? 0.f : keep_at(seq_row, t, a.L, W);
   }
-  __syncthreads();
   const int64_t c0 = ((int64_t)blockIdx.x * CL_THREADS + threadIdx.x) * V;
-  if (c0 >= a.dim) return;
-  const T* xp = (const T*)a.x + bi * a.xb + c0;
-  TO* op = (TO*)a.out + bi * a.ob + c0;
+  const bool active = c0 < a.dim;
+  const T* xp = (const T*)a.x + bi * a.xb + (active ? c0 : 0);
+  uint4 raw[NL];
+#pragma unroll
+  for (int i = 0; i < NL; ++i) {
+    // clamped, unconditional loads (a conditional load would wait at its merge)
+    const int64_t t = min(max(t0 - (W - 1) + i, (int64_t)0), a.L - 1);
+    raw[i] = __ldg(reinterpret_cast<const uint4*>(xp + t * a.xt));
+  }
   float w[V][W], bias[V];
 #pragma unroll
   for (int k = 0; k < V; ++k) {
 #pragma unroll
-    for (int j = 0; j < W; ++j) w[k][j] = __ldg(a.w + (c0 + k) * W + j);
-    bias[k] = a.bias ? __ldg(a.bias + c0 + k) : 0.f;
+    for (int j = 0; j < W; ++j) w[k][j] = active ? __ldg(a.w + (c0 + k) * W + j) : 0.f;
+    bias[k] = (active && a.bias) ? __ldg(a.bias + c0 + k) : 0.f;
   }
-  // window of the W-1 inputs before the current token, masked
+  __syncthreads();
+  if (!active) return;
+  TO* op = (TO*)a.out + bi * a.ob + c0;
+  // window of the W-1 masked inputs before the current token
   float win[W > 1 ? W - 1 : 1][V];
 #pragma unroll
   for (int j = 0; j < W - 1; ++j) {
-    const int64_t t = t0 - (W - 1) + j;
-    const float kj = keep[j];
-    if (t >= 0) {
-      float v[V];
-      load_vec<T, V>(xp + t * a.xt, v);
+    float v[V];
+    unpack_vec<T, V>(raw[j], v);
 #pragma unroll
-      for (int k = 0; k < V; ++k) win[j][k] = v[k] * kj;
-    } else {
-#pragma unroll
-      for (int k = 0; k < V; ++k) win[j][k] = 0.f;
-    }
+    for (int k = 0; k < V; ++k) win[j][k] = t0 - (W - 1) + j < 0 ? 0.f : v[k] * keep[j];
   }
-  for (int64_t i0 = 0; i0 < nt; i0 += CL_UNROLL) {
-    float xv[CL_UNROLL][V];
 #pragma unroll
-    for (int u = 0; u < CL_UNROLL; ++u) {
-      // unconditional clamped load (a conditional one would wait at its merge)
-      const int64_t t = t0 + min(i0 + u, nt - 1);
-      load_vec<T, V>(xp + t * a.xt, xv[u]);
+  for (int i = 0; i < CL_RUN; ++i) {
+    if (i >= nt) break;
+    const float kc = keep[i + W - 1];
+    float xv[V], o[V];
+    unpack_vec<T, V>(raw[i + W - 1], xv);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const float xc = xv[k] * kc;
+      float acc = bias[k];
+#pragma unroll
+      for (int j = 0; j < W - 1; ++j) acc = fmaf(w[k][j], win[j][k], acc);
+      acc = fmaf(w[k][W - 1], xc, acc);
+      o[k] = act(acc, a.silu);
+#pragma unroll
+      for (int j = 0; j + 1 < W - 1; ++j) win[j][k] = win[j + 1][k];
+      if (W > 1) win[W > 1 ? W - 2 : 0][k] = xc;
     }
-#pragma unroll
-    for (int u = 0; u < CL_UNROLL; ++u) {
-      if (i0 + u >= nt) break;
-      const float kc = keep[i0 + u + W - 1];
-      float o[V];
-#pragma unroll
-      for (int k = 0; k < V; ++k) {
-        const float xc = xv[u][k] * kc;
-        float acc = bias[k];
-#pragma unroll
-        for (int j = 0; j < W - 1; ++j) acc = fmaf(w[k][j], win[j][k], acc);
-        acc = fmaf(w[k][W - 1], xc, acc);
-        o[k] = act(acc, a.silu);
-#pragma unroll
-        for (int j = 0; j + 1 < W - 1; ++j) win[j][k] = win[j + 1][k];
-        if (W > 1) win[W > 1 ? W - 2 : 0][k] = xc;
-      }
-      store_vec<TO, V>(op + (t0 + i0 + u) * a.ot, o);
-    }
+    store_vec<TO, V>(op + (t0 + i) * a.ot, o);
   }
 }
 

@@ -94,7 +94,7 @@ def test_capi_conv_rejects_bad_args():
 # GPU
 # ---------------------------------------------------------------------------
 def _round(a, dtype):
-    return R.round_bf16(a) if dtype == torch.bfloat16 else np.asarray(a, np.float64)
+    return R.round_bf16(a) if dtype == torch.bfloat16 else np.asarray(a, np.float32).astype(np.float64)
 
 
 def _seq(b, L, rng):

@@ -74,7 +74,7 @@ def test_capi_rms_norm_rejects_bad_args():
 # GPU
 # ---------------------------------------------------------------------------
 def _round(a, dtype):
-    return R.round_bf16(a) if dtype == torch.bfloat16 else np.asarray(a, np.float64)
+    return R.round_bf16(a) if dtype == torch.bfloat16 else np.asarray(a, np.float32).astype(np.float64)
 
 
 DT = {"f32": torch.float32, "bf16": torch.bfloat16}
