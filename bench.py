@@ -8,7 +8,8 @@ Q=128, bf16 inputs, initial states in, final states out).  At N GPUs every rank 
 own batch (weak scaling, no data-path collective).  `value` is measured with inputs
 resident in HBM (one CUDA graph per step, input sets rotated so consecutive steps share
 no L2 lines); `e2e` goes through the public Python API with pinned host buffers and
-host<->device copies inside the timed region.  `--impl reference` times the CPU
+host<->device copies inside the timed region (steps alternate between two streams, so one
+step's result copy overlaps the next step's input copy).  `--impl reference` times the CPU
 restatement of the reference algorithm (the reference itself needs JAX, absent here).
 """
 from __future__ import annotations
@@ -140,13 +141,20 @@ def fwd_kwargs(cfg, d):
                 return_final_states=cfg.return_final)
 
 
-def time_region(fn, steps, stream):
-    """Device time of `steps` calls of fn() between two events on `stream`."""
+def time_region(fn, steps, stream, side=()):
+    """Device time of `steps` calls of fn() between two events on `stream`.  Work that fn
+    puts on the `side` streams starts after the first event and ends before the second."""
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
+    for s in side:
+        s.wait_event(e0)
     for i in range(steps):
         fn(i)
+    for s in side:
+        ev = torch.cuda.Event()
+        ev.record(s)
+        stream.wait_event(ev)
     e1.record(stream)
     e1.synchronize()
     return e0.elapsed_time(e1)
@@ -287,29 +295,39 @@ def run_ours(args, cfg, rank, world, device):
     value = args.steps * cfg.tokens * world / (ms / 1e3)
     launches_per_step = runners[0].launches_per_step
 
-    # end to end through the public API: pinned host inputs -> device -> forward -> host
+    # end to end through the public API: pinned host inputs -> device -> forward -> host.
+    # Consecutive steps alternate between two streams, each with its own workspace and
+    # host result buffers, so one step's result copy (D2H) overlaps the next step's input
+    # copy (H2D): the host link runs both directions at once, as a serving loop would.
     host = {k: (None if v is None else v.cpu().pin_memory()) for k, v in sets[0].items()}
     h2d = sum(v.numel() * v.element_size() for k, v in host.items() if v is not None)
     b, L, H, P, N = cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.dstate
-    out_h = torch.empty((b, L, H, P), dtype=torch.float32).pin_memory()
-    fin_h = torch.empty((b, H, P, N), dtype=torch.float32).pin_memory() if cfg.return_final else None
-    d2h = out_h.numel() * 4 + (fin_h.numel() * 4 if fin_h is not None else 0)
-    ws = torch.empty(runners[0].workspace.numel(), device=device, dtype=torch.uint8)
+    n_lanes = 2
+    lanes = []
+    for _ in range(n_lanes):
+        lanes.append({
+            "stream": torch.cuda.Stream(device),
+            "ws": torch.empty(runners[0].workspace.numel(), device=device, dtype=torch.uint8),
+            "out": torch.empty((b, L, H, P), dtype=torch.float32).pin_memory(),
+            "fin": torch.empty((b, H, P, N), dtype=torch.float32).pin_memory() if cfg.return_final else None})
+    d2h = lanes[0]["out"].numel() * 4 + (lanes[0]["fin"].numel() * 4 if cfg.return_final else 0)
 
-    def e2e_step(_i):
-        dd = {k: (None if v is None else v.to(device, non_blocking=True)) for k, v in host.items()}
-        r = mamba_chunk_scan_combined_fwd(dd["x"], dd["dt"], dd["A"], dd["B"], dd["C"], cfg.chunk_size,
-                                          workspace=ws, bf16_mma=args.bf16_mma, **fwd_kwargs(cfg, dd))
-        if cfg.return_final:
-            out_h.copy_(r[0], non_blocking=True)
-            fin_h.copy_(r[1], non_blocking=True)
-        else:
-            out_h.copy_(r, non_blocking=True)
-    for i in range(2):
+    def e2e_step(i):
+        ln = lanes[i % n_lanes]
+        with torch.cuda.stream(ln["stream"]):
+            dd = {k: (None if v is None else v.to(device, non_blocking=True)) for k, v in host.items()}
+            r = mamba_chunk_scan_combined_fwd(dd["x"], dd["dt"], dd["A"], dd["B"], dd["C"], cfg.chunk_size,
+                                              workspace=ln["ws"], bf16_mma=args.bf16_mma, **fwd_kwargs(cfg, dd))
+            if cfg.return_final:
+                ln["out"].copy_(r[0], non_blocking=True)
+                ln["fin"].copy_(r[1], non_blocking=True)
+            else:
+                ln["out"].copy_(r, non_blocking=True)
+    for i in range(2 * n_lanes):
         e2e_step(i)
     if world > 1:
         torch.distributed.barrier()
-    ms_e2e = time_region(e2e_step, args.steps, stream)
+    ms_e2e = time_region(e2e_step, args.steps, stream, side=[ln["stream"] for ln in lanes])
     t = torch.tensor([ms_e2e], device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
