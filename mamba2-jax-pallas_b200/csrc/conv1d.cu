@@ -114,12 +114,36 @@ __global__ void __launch_bounds__(CL_THREADS) conv1d_cl_kernel(const ConvArgs a)
     const int64_t t = min(max(t0 - (W - 1) + i, (int64_t)0), a.L - 1);
     raw[i] = __ldg(reinterpret_cast<const uint4*>(xp + t * a.xt));
   }
+  // this thread's V*W weights and V biases are contiguous: 16-byte loads (scalar loads at
+  // a 4*W-float lane stride cost one L1 wavefront per lane and saturated L1)
   float w[V][W], bias[V];
+  {
+    const int64_t cw = active ? c0 : 0;
+    const float4* w4 = reinterpret_cast<const float4*>(a.w + cw * W);
+    float wf[V * W];
 #pragma unroll
-  for (int k = 0; k < V; ++k) {
+    for (int q = 0; q < V * W / 4; ++q) {
+      const float4 t = __ldg(w4 + q);
+      wf[4 * q] = t.x; wf[4 * q + 1] = t.y; wf[4 * q + 2] = t.z; wf[4 * q + 3] = t.w;
+    }
 #pragma unroll
-    for (int j = 0; j < W; ++j) w[k][j] = active ? __ldg(a.w + (c0 + k) * W + j) : 0.f;
-    bias[k] = (active && a.bias) ? __ldg(a.bias + c0 + k) : 0.f;
+    for (int k = 0; k < V; ++k)
+#pragma unroll
+      for (int j = 0; j < W; ++j) w[k][j] = wf[k * W + j];
+    float bf[V];
+    if (a.bias) {
+      const float4* b4 = reinterpret_cast<const float4*>(a.bias + cw);
+#pragma unroll
+      for (int q = 0; q < V / 4; ++q) {
+        const float4 t = __ldg(b4 + q);
+        bf[4 * q] = t.x; bf[4 * q + 1] = t.y; bf[4 * q + 2] = t.z; bf[4 * q + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) bf[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) bias[k] = bf[k];
   }
   __syncthreads();
   if (!active) return;
@@ -231,6 +255,7 @@ cudaError_t launch_conv_typed(const ConvArgs& a, int64_t batch, cudaStream_t st)
   if constexpr (sizeof(TO) == 4 || V % 8 == 0) {
     const bool cl = a.xd == 1 && a.od == 1 && a.width <= 4 && a.dim % V == 0 &&
                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.bias) & 15) == 0 &&
                     a.xb % V == 0 && a.xt % V == 0 && a.ob % V == 0 && a.ot % V == 0;
     if (cl) return launch_cl<T, TO>(a, batch, st);
   }
