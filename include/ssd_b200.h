@@ -282,6 +282,34 @@ typedef struct ssd_rms_norm_params {
  * mixer at src/mamba2_jax/modules/mamba2.py:401-406 with group_size = d_ssm / ngroups. */
 int ssd_rms_norm_gated(const ssd_rms_norm_params_t* p, ssd_stream_t stream);
 
+/* Sequence-parallel decay fix-up.  A rank that ran its token segment (b, L) of a longer
+ * sequence from a zero initial state adds the state S entering the segment, received from
+ * the ranks before it, in place:
+ *   out[b,t,h,:] += exp(dA(t)) * (C[b,t,g,:] . S[b,h,:,:]^T) * silu(z[b,t,h,:])  (z optional)
+ *     for t < carried_len[b] (the tokens of the sequence carried into the segment; NULL
+ *     means all L tokens),
+ *   final_states[b,h] += exp(dA(L-1)) * S[b,h]   when carried_len[b] >= L (optional),
+ * where dA(t) is the segment-wide cumulative sum of dt*A, read from the segment's
+ * chunk_cumsum output (b,H,nc,Q).  headdim must be a multiple of 4. */
+typedef struct ssd_sp_fixup_params {
+  int64_t batch, seqlen, nheads, headdim, ngroups, dstate, chunk_size;
+  int32_t dtype;              /* ssd_dtype_t of C and z */
+  int32_t reserved;
+  const void* C;              /* (b,L,G,N) */
+  const void* z;              /* (b,L,H,P) or NULL */
+  const float* dA_cumsum;     /* (b,H,nc,Q) within-chunk cumsum of dt*A */
+  const float* state_in;      /* (b,H,P,N) */
+  const int32_t* carried_len; /* (b,) or NULL */
+  float* out;                 /* (b,L,H,P), updated in place */
+  float* final_states;        /* (b,H,P,N), updated in place, or NULL */
+} ssd_sp_fixup_params_t;
+
+/* The decay fix-up of the optional sequence-parallel mode.  The reference has no
+ * sequence parallelism; this applies the state-passing recurrence of
+ * src/mamba2_jax/kernels/state_passing_fwd.py:108-151 and the inter-chunk term of
+ * src/mamba2_jax/kernels/chunk_scan_fwd.py:108-232 across a segment boundary. */
+int ssd_sp_state_fixup(const ssd_sp_fixup_params_t* p, ssd_stream_t stream);
+
 /* Thread-local description of the last failure on this host thread ("" if none). */
 const char* ssd_last_error(void);
 

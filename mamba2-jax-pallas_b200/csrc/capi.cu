@@ -399,4 +399,20 @@ int ssd_rms_norm_gated(const ssd_rms_norm_params_t* p, ssd_stream_t stream) {
   return cuda_status(ssd::launch_rms_norm_gated(p, (cudaStream_t)stream), "rms_norm_gated");
 }
 
+int ssd_sp_state_fixup(const ssd_sp_fixup_params_t* p, ssd_stream_t stream) {
+  g_err[0] = 0;
+  if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
+  if (p->batch <= 0 || p->seqlen <= 0 || p->nheads <= 0 || p->headdim <= 0 || p->ngroups <= 0 ||
+      p->dstate <= 0 || p->chunk_size <= 0)
+    return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
+  if (p->nheads % p->ngroups != 0) return fail(SSD_ERR_INVALID_ARG, "nheads must be a multiple of ngroups");
+  if (p->headdim % 4 != 0) return fail(SSD_ERR_UNSUPPORTED, "headdim must be a multiple of 4");
+  if (ssd::sp_fixup_smem_bytes(p->headdim, p->dstate) > 227 * 1024)
+    return fail(SSD_ERR_UNSUPPORTED, "headdim * dstate too large for the fix-up's shared memory");
+  if (!dtype_ok(p->dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (!p->C || !p->dA_cumsum || !p->state_in || !p->out)
+    return fail(SSD_ERR_INVALID_ARG, "C, dA_cumsum, state_in and out are required");
+  return cuda_status(ssd::launch_sp_fixup(p, (cudaStream_t)stream), "sp_state_fixup");
+}
+
 }  // extern "C"

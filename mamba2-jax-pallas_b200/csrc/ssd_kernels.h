@@ -35,6 +35,8 @@ cudaError_t launch_ssu(const ssu_params_t* p, cudaStream_t st);
 cudaError_t launch_conv1d(const ssd_conv1d_params_t* p, cudaStream_t st);
 cudaError_t launch_conv1d_update(const ssd_conv1d_update_params_t* p, cudaStream_t st);
 cudaError_t launch_rms_norm_gated(const ssd_rms_norm_params_t* p, cudaStream_t st);
+cudaError_t launch_sp_fixup(const ssd_sp_fixup_params_t* p, cudaStream_t st);
+size_t sp_fixup_smem_bytes(int64_t P, int64_t N);
 
 // Set the thread-local message ssd_last_error() returns.
 void set_last_error(const char* msg);

@@ -33,7 +33,7 @@ EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
             "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_combined_fwd_noalloc", "ssd_chunk_cumsum_fwd",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
-            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_last_error", "ssd_abi_version"]
+            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_sp_state_fixup", "ssd_last_error", "ssd_abi_version"]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -85,6 +85,14 @@ class RmsNormParams(ctypes.Structure):
                 ("x", _vp), ("z", _vp), ("weight", _vp), ("out", _vp)]
 
 
+class SpFixupParams(ctypes.Structure):
+    _fields_ = [("batch", _i64), ("seqlen", _i64), ("nheads", _i64), ("headdim", _i64),
+                ("ngroups", _i64), ("dstate", _i64), ("chunk_size", _i64),
+                ("dtype", _i32), ("reserved", _i32),
+                ("C", _vp), ("z", _vp), ("dA_cumsum", _vp), ("state_in", _vp), ("carried_len", _vp),
+                ("out", _vp), ("final_states", _vp)]
+
+
 class SsdError(RuntimeError):
     """A non-zero ssd_status_t from the library."""
 
@@ -128,6 +136,7 @@ def load() -> ctypes.CDLL:
     lib.ssd_causal_conv1d_fwd.argtypes = [P(Conv1dParams), _vp]
     lib.ssd_causal_conv1d_update.argtypes = [P(Conv1dUpdateParams), _vp]
     lib.ssd_rms_norm_gated.argtypes = [P(RmsNormParams), _vp]
+    lib.ssd_sp_state_fixup.argtypes = [P(SpFixupParams), _vp]
     lib.ssd_chunk_state_varlen_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _i32,
                                                _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
     lib.ssd_selective_state_update.argtypes = [P(SsuParams), _vp]

@@ -13,9 +13,9 @@ inside it cuts the carried state) and state s computed from a zero initial state
 combine (a1, s1) o (a2, s2) = (a1 a2, a2 s1 + s2) is associative, so each rank needs the
 exclusive prefix of the pairs of the ranks before it.  That prefix is exchanged by
 recursive doubling with point-to-point sends (log2(world) rounds of (b,H) + (b,H,P,N)
-fp32 per rank), then every rank reruns its segment with the received state as its
-initial state; with packed sequences only the chunks that hold the carried sequence are
-rerun.  The exchange is the only collective of the path.
+fp32 per rank).  The received state's contribution is then added by one fix-up launch
+(exp(dA) C S^T on the carried sequence's tokens, exp(total dA) S on the final state)
+instead of a second forward.  The exchange is the only collective of the path.
 """
 from __future__ import annotations
 
@@ -140,11 +140,13 @@ def _peer(r, group):
 
 
 def segment_decay(dt, A, chunk_size, dt_bias=None, dt_softplus=False, dt_limit=(0.0, math.inf),
-                  seq_idx=None, carried_seq=None):
+                  seq_idx=None, carried_seq=None, dA_cumsum=None):
     """Total decay (b,H) of a token segment: exp(sum_t dt'_t A), or 0 for batch rows whose
     last token belongs to another sequence than the carried one (seq_idx given)."""
     from .kernels import chunk_cumsum_fwd
-    dA, _ = chunk_cumsum_fwd(dt, A, chunk_size, dt_bias=dt_bias, dt_softplus=dt_softplus, dt_limit=dt_limit)
+    dA = dA_cumsum
+    if dA is None:
+        dA, _ = chunk_cumsum_fwd(dt, A, chunk_size, dt_bias=dt_bias, dt_softplus=dt_softplus, dt_limit=dt_limit)
     a = torch.exp(dA[..., -1].sum(-1))
     if seq_idx is not None and carried_seq is not None:
         a = a * (seq_idx[:, -1] == carried_seq).to(a.dtype)[:, None]
@@ -182,42 +184,53 @@ def ssd_forward_sequence_parallel(x, dt, A, B, C, chunk_size, D=None, z=None, dt
         carried = (torch.zeros(b, dtype=torch.int32, device=x.device) if rank == 0 else prev_seq.to(torch.int32))
         sq = seq_idx.to(torch.int32) if rank == 0 else relabel_seq_idx(seq_idx, carried)
     # pass 1: this segment from a zero state, and its decay
+    from .kernels import chunk_cumsum_fwd
     init0 = initial_states if rank == 0 else None
     out0, s_loc = mamba_chunk_scan_combined_fwd(x, dt, A, B, C, chunk_size, initial_states=init0, seq_idx=sq,
                                                 return_final_states=True, **kw)
-    a_loc = segment_decay(dt, A, chunk_size, dt_bias, dt_softplus, dt_limit, sq,
-                          None if sq is None else torch.zeros_like(carried))
+    dA, _ = chunk_cumsum_fwd(dt, A, chunk_size, dt_bias=dt_bias, dt_softplus=dt_softplus, dt_limit=dt_limit)
+    a_loc = segment_decay(dt, A, chunk_size, seq_idx=sq,
+                          carried_seq=None if sq is None else torch.zeros_like(carried), dA_cumsum=dA)
     if rank == 0:
         a_loc = torch.zeros_like(a_loc)   # rank 0's pair already holds the initial state
     # exchange: the state entering this segment
     _, s_in = exclusive_prefix(a_loc.float().contiguous(), s_loc.float().contiguous(), group)
     if rank == 0:
         return out0, s_loc   # pass 1 already started from the sequence's initial state
-    # pass 2: the segment with the received state (applies to the carried sequence, id 0)
-    lp = carried_prefix(sq, chunk_size) if sq is not None else L
-    if lp == 0:
-        return out0, s_loc   # the segment starts a new sequence: the state does not enter
-    if lp >= L:
-        return mamba_chunk_scan_combined_fwd(x, dt, A, B, C, chunk_size, initial_states=s_in.contiguous(),
-                                             seq_idx=sq, return_final_states=True, **kw)
-    # The carried sequence ends inside the first lp tokens of every batch row: only those
-    # chunks see the received state.  The later tokens and the final state (which decays
-    # through a sequence reset to exactly 0 before them) are pass 1's.
-    sl = lambda t: None if t is None else t[:, :lp]
-    kw2 = dict(kw, z=sl(z))
-    out_p, _ = mamba_chunk_scan_combined_fwd(sl(x), sl(dt), A, sl(B), sl(C), chunk_size,
-                                             initial_states=s_in.contiguous(), seq_idx=sl(sq),
-                                             return_final_states=True, **kw2)
-    out0[:, :lp] = out_p
+    # fix-up: add the received state's contribution to the carried sequence's tokens (and
+    # to the final state when that sequence reaches the segment's end), in place
+    clen = None if sq is None else carried_len(sq)
+    sp_state_fixup(out0, C, z, dA, s_in, chunk_size, carried=clen, final_states=s_loc)
     return out0, s_loc
 
 
-def carried_prefix(seq_idx: torch.Tensor, chunk_size: int) -> int:
-    """Tokens of a segment, rounded up to whole chunks, that hold the carried sequence (id 0
-    after relabel_seq_idx) in every batch row: the first position with another id, maxed
-    over rows (the segment length if some row never leaves it)."""
+def carried_len(seq_idx: torch.Tensor) -> torch.Tensor:
+    """(b,) int32: per batch row, the number of leading tokens of the carried sequence (id 0
+    after relabel_seq_idx), i.e. the first position with another id, or the segment length."""
     b, L = seq_idx.shape
     other = seq_idx != 0
     first = torch.where(other.any(1), other.int().argmax(1), torch.full((b,), L, device=seq_idx.device))
-    t_end = int(first.max().item())
-    return min(L, -(-t_end // chunk_size) * chunk_size)
+    return first.to(torch.int32).contiguous()
+
+
+def sp_state_fixup(out, C, z, dA_cumsum, state_in, chunk_size, carried=None, final_states=None):
+    """In place: out[b,t,h] += exp(dA(t)) C[b,t,g] . state_in[b,h]^T (times silu(z)) for the
+    carried tokens, and final_states += exp(dA(L-1)) state_in where the carried sequence
+    reaches the segment's end.  One launch of ``ssd_sp_state_fixup``."""
+    from . import _lib
+    b, L, H, P = out.shape
+    G, N = C.shape[2], C.shape[3]
+    if out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 tensor")
+    if final_states is not None and (final_states.dtype != torch.float32 or not final_states.is_contiguous()):
+        raise ValueError("final_states must be a contiguous float32 tensor")
+    Cc = _lib.dev(C, "C")
+    zc = _lib.dev(z, "z", Cc.dtype)
+    dAc = _lib.dev(dA_cumsum, "dA_cumsum", torch.float32)
+    sc = _lib.dev(state_in, "state_in", torch.float32)
+    cl = _lib.dev(carried, "carried", torch.int32)
+    p = _lib.SpFixupParams(batch=b, seqlen=L, nheads=H, headdim=P, ngroups=G, dstate=N, chunk_size=chunk_size,
+                           dtype=_lib.dtype_code(Cc))
+    p.C, p.z, p.dA_cumsum, p.state_in = Cc.data_ptr(), _lib.ptr(zc), dAc.data_ptr(), sc.data_ptr()
+    p.carried_len, p.out, p.final_states = _lib.ptr(cl), out.data_ptr(), _lib.ptr(final_states)
+    _lib.check(_lib.load().ssd_sp_state_fixup(p, _lib.stream_of(out)))

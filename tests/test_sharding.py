@@ -163,15 +163,24 @@ def test_sequence_parallel_algorithm_matches_oracle(world, lens):
             outs.append(out_loc)
             a = np.zeros_like(a)
         else:
-            # rerun with the received state, only over the chunks holding the carried sequence
-            lp = L if sq is None else SH.carried_prefix(torch.from_numpy(sq), Q)
+            # fix-up: the received state's term on the carried tokens (what the CUDA fix-up does)
+            clen = (t1 - t0) if sq is None else int(SH.carried_len(torch.from_numpy(sq))[0])
             o2 = out_loc.copy()
-            if lp > 0:
-                pre = {k: (v[:, :lp] if k in ("x", "dt", "B", "C", "z") and v is not None else v)
-                       for k, v in sin.items()}
-                o2[:, :lp] = _oracle(pre, Q, acc_s, None if sq is None else sq[:, :lp])[0]
+            seg_L = t1 - t0
+            dt_full = R.chunk_cumsum(sin["dt"], inp["A"], seg_L, inp["dt_bias"], True)[0][..., 0, :seg_L]
+            hpg = 4 // 2
+            for t in range(clen):
+                for h in range(4):
+                    g = h // hpg
+                    y = np.exp(dt_full[0, h, t]) * (acc_s[0, h] @ sin["C"][0, t, g])
+                    o2[0, t, h] += y * R.silu(np.float64(sin["z"][0, t, h]))
             outs.append(o2)
-        acc_a, acc_s = acc_a * a, a[..., None, None] * acc_s + s_loc
+            if clen == seg_L:
+                s_loc = s_loc + np.exp(dt_full[0, :, seg_L - 1])[:, None, None] * acc_s[0][None]
+        if r == 0:
+            acc_a, acc_s = acc_a * a, a[..., None, None] * acc_s + s_loc
+        else:
+            acc_a, acc_s = acc_a * a, s_loc      # s_loc already carries the received state
     np.testing.assert_allclose(np.concatenate(outs, 1), full_out, rtol=1e-9, atol=1e-9)
     np.testing.assert_allclose(acc_s, full_final, rtol=1e-9, atol=1e-9)
 
@@ -215,12 +224,11 @@ def test_sequence_parallel_forward_two_ranks_one_gpu(lens):
         assert res[r][1] <= 1e-2, (r, res[r])
 
 
-def test_carried_prefix():
+def test_carried_len():
     sq = torch.tensor([[0, 0, 0, 1, 1, 2, 2, 2], [0, 0, 0, 0, 0, 1, 1, 1]], dtype=torch.int32)
-    assert SH.carried_prefix(sq, 2) == 6       # row 1 leaves at 5 -> 3 chunks
-    assert SH.carried_prefix(sq[:1], 4) == 4
-    assert SH.carried_prefix(torch.zeros((1, 8), dtype=torch.int32), 4) == 8
-    assert SH.carried_prefix(torch.ones((1, 8), dtype=torch.int32), 4) == 0
+    assert SH.carried_len(sq).tolist() == [3, 5]
+    assert SH.carried_len(torch.zeros((1, 8), dtype=torch.int32)).tolist() == [8]
+    assert SH.carried_len(torch.ones((1, 8), dtype=torch.int32)).tolist() == [0]
 
 
 @pytest.mark.gpu
@@ -246,3 +254,40 @@ def test_head_sharded_outputs_bitwise_equal(world):
         o, f = run(SH.shard_heads(d, world, r))
         assert torch.equal(o, out[:, :, h0:h1])
         assert torch.equal(f, fin[:, h0:h1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,N,Q,lens", [("bf16", 128, 128, None), ("bf16", 256, 128, [[700, 324], [100, 924]]),
+                                            ("f32", 128, 64, [[1024], [333, 691]]), ("bf16", 128, 256, [[0, 1024], [512, 512]])],
+                         ids=["one-seq", "n256-packed", "f32-q64", "new-seq-first"])
+def test_sp_fixup_equals_forward_with_initial_state(dtype, N, Q, lens):
+    """Zero-state forward + ssd_sp_state_fixup(S) equals the forward started from S, for
+    out and final states; per batch row the carried sequence ends at a different token."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from gpu_util import TOL, dev_inputs, rel_l2, to_dev
+    from mamba2_b200 import chunk_cumsum_fwd, mamba_chunk_scan_combined_fwd
+    L, H, P, G = 1024, 8, 64, 2
+    cfg = S.SsdConfig("fx", 2, L, H, P, G, N, Q, dtype, has_z=True, has_init=True, return_final=True)
+    d = dev_inputs(S.make_ssd_inputs(cfg, 31), dtype)
+    seq = None
+    if lens is not None:
+        seq = np.stack([np.repeat(np.arange(len(r)), r) for r in lens]).astype(np.int32)
+        if lens[0][0] == 0:
+            seq[0] += 1                       # row 0 holds no token of the carried sequence
+        seq = to_dev(seq, int32=True)
+    kw = dict(D=d["D"], z=d["z"], dt_bias=d["dt_bias"], dt_softplus=True, seq_idx=seq, return_final_states=True)
+    ref_out, ref_fin = mamba_chunk_scan_combined_fwd(d["x"], d["dt"], d["A"], d["B"], d["C"], Q,
+                                                     initial_states=d["initial_states"], **kw)
+    out, fin = mamba_chunk_scan_combined_fwd(d["x"], d["dt"], d["A"], d["B"], d["C"], Q, **kw)
+    dA, _ = chunk_cumsum_fwd(d["dt"], d["A"], Q, dt_bias=d["dt_bias"], dt_softplus=True)
+    clen = None if seq is None else SH.carried_len(seq)
+    SH.sp_state_fixup(out, d["C"], d["z"], dA, d["initial_states"], Q, carried=clen, final_states=fin)
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref_out.double().cpu().numpy()) <= TOL[dtype]
+    assert rel_l2(fin, ref_fin.double().cpu().numpy()) <= TOL[dtype]
+    if seq is not None:                       # tokens after the carried sequence are untouched
+        out0, _ = mamba_chunk_scan_combined_fwd(d["x"], d["dt"], d["A"], d["B"], d["C"], Q, **kw)
+        for bi in range(2):
+            c = int(clen[bi])
+            assert torch.equal(out[bi, c:], out0[bi, c:])
