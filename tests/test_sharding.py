@@ -291,3 +291,22 @@ def test_sp_fixup_equals_forward_with_initial_state(dtype, N, Q, lens):
         for bi in range(2):
             c = int(clen[bi])
             assert torch.equal(out[bi, c:], out0[bi, c:])
+
+
+def test_capi_sp_fixup_rejects_bad_args():
+    import ctypes
+    from mamba2_b200 import _lib
+    lib = _lib.load()
+    p = _lib.SpFixupParams(batch=1, seqlen=256, nheads=8, headdim=64, ngroups=2, dstate=128, chunk_size=128)
+    assert lib.ssd_sp_state_fixup(ctypes.byref(p), None) == 1          # C, dA, state, out missing
+    p.C, p.dA_cumsum, p.state_in, p.out = 256, 512, 1024, 2048
+    p.headdim = 62
+    assert lib.ssd_sp_state_fixup(ctypes.byref(p), None) == 2          # headdim % 4
+    p.headdim, p.ngroups = 64, 3
+    assert lib.ssd_sp_state_fixup(ctypes.byref(p), None) == 1          # H % G
+    p.ngroups, p.dstate, p.headdim = 2, 1024, 128
+    assert lib.ssd_sp_state_fixup(ctypes.byref(p), None) == 2          # shared memory budget
+    assert "shared memory" in lib.ssd_last_error().decode()
+    p.dstate, p.dtype = 128, 9
+    assert lib.ssd_sp_state_fixup(ctypes.byref(p), None) == 1          # bad dtype enum
+    assert lib.ssd_sp_state_fixup(None, None) == 1
