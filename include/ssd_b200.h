@@ -227,10 +227,12 @@ typedef struct ssd_conv1d_params {
   int32_t out_dtype;      /* ssd_dtype_t of out */
   int32_t silu;           /* nonzero: activation "silu" */
   const void* x;
-  const float* weight;    /* (dim, width) f32, contiguous */
-  const float* bias;      /* (dim,) f32 or NULL */
+  const void* weight;     /* (dim, width) contiguous, f32 or bf16 (weight_dtype) */
+  const void* bias;       /* (dim,) f32 or bf16 (bias_dtype), or NULL */
   const int32_t* seq_idx; /* (batch, seqlen) contiguous, or NULL */
   void* out;              /* must not overlap x */
+  int32_t weight_dtype;   /* ssd_dtype_t of weight (0 = f32) */
+  int32_t bias_dtype;     /* ssd_dtype_t of bias (0 = f32) */
 } ssd_conv1d_params_t;
 
 /* Replaces causal_conv1d (src/mamba2_jax/ops/causal_conv1d.py:18-85). */
@@ -250,9 +252,11 @@ typedef struct ssd_conv1d_update_params {
   int32_t reserved;
   const void* x_new;      /* (batch, dim) contiguous */
   void* conv_state;
-  const float* weight;    /* (dim, width) f32, contiguous */
-  const float* bias;      /* (dim,) f32 or NULL */
+  const void* weight;     /* (dim, width) contiguous, f32 or bf16 (weight_dtype) */
+  const void* bias;       /* (dim,) f32 or bf16 (bias_dtype), or NULL */
   void* out;              /* (batch, dim) contiguous */
+  int32_t weight_dtype;   /* ssd_dtype_t of weight (0 = f32) */
+  int32_t bias_dtype;     /* ssd_dtype_t of bias (0 = f32) */
 } ssd_conv1d_update_params_t;
 
 /* Replaces causal_conv1d_update (src/mamba2_jax/ops/causal_conv1d.py:88-139); the state

@@ -366,7 +366,8 @@ int ssd_causal_conv1d_fwd(const ssd_conv1d_params_t* p, ssd_stream_t stream) {
   if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
   if (p->batch <= 0 || p->dim <= 0 || p->seqlen <= 0) return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
   if (p->width < 1 || p->width > 8) return fail(SSD_ERR_UNSUPPORTED, "width must be 1..8");
-  if (!dtype_ok(p->dtype) || !dtype_ok(p->out_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (!dtype_ok(p->dtype) || !dtype_ok(p->out_dtype) || !dtype_ok(p->weight_dtype) || !dtype_ok(p->bias_dtype))
+    return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
   if (!p->x || !p->weight || !p->out) return fail(SSD_ERR_INVALID_ARG, "x, weight and out are required");
   if (p->x == p->out) return fail(SSD_ERR_INVALID_ARG, "out must not alias x");
   return cuda_status(ssd::launch_conv1d(p, (cudaStream_t)stream), "causal_conv1d");
@@ -377,7 +378,8 @@ int ssd_causal_conv1d_update(const ssd_conv1d_update_params_t* p, ssd_stream_t s
   if (!p) return fail(SSD_ERR_INVALID_ARG, "params is NULL");
   if (p->batch <= 0 || p->dim <= 0) return fail(SSD_ERR_INVALID_ARG, "dims must be positive");
   if (p->width < 1 || p->width > 8) return fail(SSD_ERR_UNSUPPORTED, "width must be 1..8");
-  if (!dtype_ok(p->x_dtype) || !dtype_ok(p->state_dtype) || !dtype_ok(p->out_dtype))
+  if (!dtype_ok(p->x_dtype) || !dtype_ok(p->state_dtype) || !dtype_ok(p->out_dtype) ||
+      !dtype_ok(p->weight_dtype) || !dtype_ok(p->bias_dtype))
     return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
   if (!p->x_new || !p->conv_state || !p->weight || !p->out)
     return fail(SSD_ERR_INVALID_ARG, "x_new, conv_state, weight and out are required");

@@ -30,8 +30,9 @@ struct ConvArgs {
   int64_t xb, xd, xt, ob, od, ot;   // element strides
   int width, silu;
   const void* x;
-  const float* w;
-  const float* bias;
+  const void* w;
+  const void* bias;
+  int w_bf16, b_bf16;       // weight / bias stored as bf16 (else f32)
   const int32_t* seq;
   void* out;
 };
@@ -65,6 +66,34 @@ __device__ __forceinline__ void store_vec(TO* p, const float (&v)[V]) {
         u[i] = *reinterpret_cast<uint32_t*>(&h);
       }
       *reinterpret_cast<uint4*>(p + k) = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+  }
+}
+
+// Scalar weight / bias element as f32 (bf16 or f32 storage).
+__device__ __forceinline__ float wld(const void* p, int is_bf16, int64_t i) {
+  return is_bf16 ? __bfloat162float(__ldg(reinterpret_cast<const bf16*>(p) + i))
+                 : __ldg(reinterpret_cast<const float*>(p) + i);
+}
+
+// N contiguous weights as f32, 4 per load (8 bytes of bf16 or 16 bytes of f32); N % 4 == 0
+// and the start 8- (bf16) or 16-byte (f32) aligned.
+template <int N>
+__device__ __forceinline__ void wld_vec(const void* p, int is_bf16, int64_t off, float (&v)[N]) {
+  if (is_bf16) {
+    const uint2* q = reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(p) + off);
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const uint2 u = __ldg(q + i);
+      v[4 * i] = __uint_as_float(u.x << 16); v[4 * i + 1] = __uint_as_float(u.x & 0xffff0000u);
+      v[4 * i + 2] = __uint_as_float(u.y << 16); v[4 * i + 3] = __uint_as_float(u.y & 0xffff0000u);
+    }
+  } else {
+    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + off);
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      const float4 t = __ldg(q + i);
+      v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
     }
   }
 }
@@ -119,25 +148,15 @@ __global__ void __launch_bounds__(CL_THREADS) conv1d_cl_kernel(const ConvArgs a)
   float w[V][W], bias[V];
   {
     const int64_t cw = active ? c0 : 0;
-    const float4* w4 = reinterpret_cast<const float4*>(a.w + cw * W);
     float wf[V * W];
-#pragma unroll
-    for (int q = 0; q < V * W / 4; ++q) {
-      const float4 t = __ldg(w4 + q);
-      wf[4 * q] = t.x; wf[4 * q + 1] = t.y; wf[4 * q + 2] = t.z; wf[4 * q + 3] = t.w;
-    }
+    wld_vec<V * W>(a.w, a.w_bf16, cw * W, wf);
 #pragma unroll
     for (int k = 0; k < V; ++k)
 #pragma unroll
       for (int j = 0; j < W; ++j) w[k][j] = wf[k * W + j];
     float bf[V];
     if (a.bias) {
-      const float4* b4 = reinterpret_cast<const float4*>(a.bias + cw);
-#pragma unroll
-      for (int q = 0; q < V / 4; ++q) {
-        const float4 t = __ldg(b4 + q);
-        bf[4 * q] = t.x; bf[4 * q + 1] = t.y; bf[4 * q + 2] = t.z; bf[4 * q + 3] = t.w;
-      }
+      wld_vec<V>(a.bias, a.b_bf16, cw, bf);
     } else {
 #pragma unroll
       for (int k = 0; k < V; ++k) bf[k] = 0.f;
@@ -187,11 +206,11 @@ __global__ void __launch_bounds__(GEN_THREADS) conv1d_generic_kernel(const ConvA
   const int64_t t = idx % a.L, d = (idx / a.L) % a.dim, bi = idx / (a.L * a.dim);
   const int32_t* seq_row = a.seq ? a.seq + bi * a.L : nullptr;
   const T* xp = (const T*)a.x + bi * a.xb + d * a.xd;
-  float acc = a.bias ? a.bias[d] : 0.f;
+  float acc = a.bias ? wld(a.bias, a.b_bf16, d) : 0.f;
   for (int j = 0; j < a.width; ++j) {
     const int64_t s = t - (a.width - 1) + j;
     if (s < 0) continue;
-    acc = fmaf(a.w[d * a.width + j], ldg(xp + s * a.xt) * keep_at(seq_row, s, a.L, a.width), acc);
+    acc = fmaf(wld(a.w, a.w_bf16, d * a.width + j), ldg(xp + s * a.xt) * keep_at(seq_row, s, a.L, a.width), acc);
   }
   st((TO*)a.out + bi * a.ob + d * a.od + t * a.ot, act(acc, a.silu));
 }
@@ -201,8 +220,9 @@ struct UpdArgs {
   int width, silu;
   const void* x;
   void* state;
-  const float* w;
-  const float* bias;
+  const void* w;
+  const void* bias;
+  int w_bf16, b_bf16;
   void* out;
 };
 
@@ -222,12 +242,12 @@ __global__ void __launch_bounds__(GEN_THREADS) conv1d_update_kernel(const UpdArg
     st(&xs, ldg((const TX*)a.x + idx));
     v[a.width - 1 < MAX_WIDTH ? a.width - 1 : 0] = ld(&xs);
   }
-  float acc = a.bias ? a.bias[d] : 0.f;
+  float acc = a.bias ? wld(a.bias, a.b_bf16, d) : 0.f;
 #pragma unroll
   for (int j = 0; j < MAX_WIDTH; ++j) {
     if (j < a.width) {
       st(s + j, v[j]);
-      acc = fmaf(a.w[d * a.width + j], v[j], acc);
+      acc = fmaf(wld(a.w, a.w_bf16, d * a.width + j), v[j], acc);
     }
   }
   st((TO*)a.out + idx, act(acc, a.silu));
@@ -275,6 +295,7 @@ cudaError_t launch_conv1d(const ssd_conv1d_params_t* p, cudaStream_t st) {
   a.ob = p->out_stride_b; a.od = p->out_stride_d; a.ot = p->out_stride_t;
   a.width = p->width; a.silu = p->silu != 0;
   a.x = p->x; a.w = p->weight; a.bias = p->bias; a.seq = p->seq_idx; a.out = p->out;
+  a.w_bf16 = p->weight_dtype == SSD_DTYPE_BF16; a.b_bf16 = p->bias_dtype == SSD_DTYPE_BF16;
   const bool xf = p->dtype == SSD_DTYPE_F32, of = p->out_dtype == SSD_DTYPE_F32;
   if (xf && of) return launch_conv_typed<float, float>(a, p->batch, st);
   if (xf) return launch_conv_typed<float, bf16>(a, p->batch, st);
@@ -287,6 +308,7 @@ cudaError_t launch_conv1d_update(const ssd_conv1d_update_params_t* p, cudaStream
   a.batch = p->batch; a.dim = p->dim; a.sb = p->state_stride_b; a.sd = p->state_stride_d;
   a.width = p->width; a.silu = p->silu != 0;
   a.x = p->x_new; a.state = p->conv_state; a.w = p->weight; a.bias = p->bias; a.out = p->out;
+  a.w_bf16 = p->weight_dtype == SSD_DTYPE_BF16; a.b_bf16 = p->bias_dtype == SSD_DTYPE_BF16;
   const unsigned grid = (unsigned)((p->batch * p->dim + GEN_THREADS - 1) / GEN_THREADS);
   const int code = (p->x_dtype == SSD_DTYPE_F32 ? 4 : 0) + (p->state_dtype == SSD_DTYPE_F32 ? 2 : 0) +
                    (p->out_dtype == SSD_DTYPE_F32 ? 1 : 0);

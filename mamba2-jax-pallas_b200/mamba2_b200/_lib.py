@@ -67,14 +67,16 @@ class Conv1dParams(ctypes.Structure):
                 ("x_stride_b", _i64), ("x_stride_d", _i64), ("x_stride_t", _i64),
                 ("out_stride_b", _i64), ("out_stride_d", _i64), ("out_stride_t", _i64),
                 ("width", _i32), ("dtype", _i32), ("out_dtype", _i32), ("silu", _i32),
-                ("x", _vp), ("weight", _vp), ("bias", _vp), ("seq_idx", _vp), ("out", _vp)]
+                ("x", _vp), ("weight", _vp), ("bias", _vp), ("seq_idx", _vp), ("out", _vp),
+                ("weight_dtype", _i32), ("bias_dtype", _i32)]
 
 
 class Conv1dUpdateParams(ctypes.Structure):
     _fields_ = [("batch", _i64), ("dim", _i64), ("state_stride_b", _i64), ("state_stride_d", _i64),
                 ("width", _i32), ("x_dtype", _i32), ("state_dtype", _i32), ("out_dtype", _i32),
                 ("silu", _i32), ("reserved", _i32),
-                ("x_new", _vp), ("conv_state", _vp), ("weight", _vp), ("bias", _vp), ("out", _vp)]
+                ("x_new", _vp), ("conv_state", _vp), ("weight", _vp), ("bias", _vp), ("out", _vp),
+                ("weight_dtype", _i32), ("bias_dtype", _i32)]
 
 
 class RmsNormParams(ctypes.Structure):

@@ -22,6 +22,14 @@ def _weight2d(weight: torch.Tensor) -> torch.Tensor:
     return weight
 
 
+def _param(t, name):
+    """Weight or bias as stored (f32 or bf16 are read by the kernels directly; other
+    dtypes are cast to f32), contiguous, on the device."""
+    if t is None:
+        return None
+    return _lib.dev(t, name, None if t.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+
+
 def _promote(*ts) -> torch.dtype:
     dt = ts[0].dtype
     for t in ts[1:]:
@@ -58,8 +66,8 @@ def causal_conv1d(x, weight, bias=None, activation=None, seq_idx=None):
         out = torch.empty((b, L, d), device=x.device, dtype=out_dtype).transpose(1, 2)
     else:
         out = torch.empty((b, d, L), device=x.device, dtype=out_dtype)
-    wt = _lib.dev(w, "weight", torch.float32)
-    bt = _lib.dev(bias, "bias", torch.float32)
+    wt = _param(w, "weight")
+    bt = _param(bias, "bias")
     sq = _lib.dev(seq_idx, "seq_idx", torch.int32)
     p = _lib.Conv1dParams(batch=b, dim=d, seqlen=L,
                           x_stride_b=x.stride(0), x_stride_d=x.stride(1), x_stride_t=x.stride(2),
@@ -68,6 +76,7 @@ def causal_conv1d(x, weight, bias=None, activation=None, seq_idx=None):
                           out_dtype=_lib.dtype_code(out), silu=int(activation == "silu"))
     p.x, p.weight, p.bias = x.data_ptr(), wt.data_ptr(), _lib.ptr(bt)
     p.seq_idx, p.out = _lib.ptr(sq), out.data_ptr()
+    p.weight_dtype, p.bias_dtype = _lib.dtype_code(wt), (_lib.dtype_code(bt) if bt is not None else 0)
     _lib.check(_lib.load().ssd_causal_conv1d_fwd(p, _lib.stream_of(out)))
     return out
 
@@ -101,12 +110,13 @@ def causal_conv1d_update(x_new, conv_state, weight, bias=None, activation=None, 
     out_dtype = _promote(st, w, bias)
     out = torch.empty((b, d), device=conv_state.device, dtype=out_dtype)
     xt = _lib.dev(x_new, "x_new")
-    wt = _lib.dev(w, "weight", torch.float32)
-    bt = _lib.dev(bias, "bias", torch.float32)
+    wt = _param(w, "weight")
+    bt = _param(bias, "bias")
     p = _lib.Conv1dUpdateParams(batch=b, dim=d, state_stride_b=st.stride(0), state_stride_d=st.stride(1),
                                 width=k, x_dtype=_lib.dtype_code(xt), state_dtype=_lib.dtype_code(st),
                                 out_dtype=_lib.dtype_code(out), silu=int(activation == "silu"))
     p.x_new, p.conv_state, p.weight = xt.data_ptr(), st.data_ptr(), wt.data_ptr()
     p.bias, p.out = _lib.ptr(bt), out.data_ptr()
+    p.weight_dtype, p.bias_dtype = _lib.dtype_code(wt), (_lib.dtype_code(bt) if bt is not None else 0)
     _lib.check(_lib.load().ssd_causal_conv1d_update(p, _lib.stream_of(out)))
     return st, out
