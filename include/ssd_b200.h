@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define SSD_B200_ABI_VERSION 1
+#define SSD_B200_ABI_VERSION 2
 
 typedef enum ssd_status {
   SSD_OK = 0,
@@ -90,9 +90,29 @@ typedef struct ssd_fwd_params {
                                     reference's Pallas kernels do for fp32 inputs (bf16 MMA
                                     operands, fp32 accumulation); without it fp32 inputs run
                                     exact fp32 on the CUDA cores */
+#define SSD_FLAG_TEST_WAIT_TIMEOUT 8  /* test only: every CTA of the fused tensor-core kernel
+                                    first runs a short bounded wait on a barrier that nothing
+                                    arrives on, so the wait gives up, the status word records
+                                    SSD_ERR_TIMEOUT and the launch does no work (checks the
+                                    timeout report without faulting anything) */
 
-/* Bytes of device workspace ssd_combined_fwd needs for these params. */
+/* Bytes of device workspace ssd_combined_fwd needs for these params; 0 when the params are
+ * invalid (ssd_combined_fwd then reports why).  The first 4 bytes of every workspace are the
+ * device status word (see ssd_status_copy_async). */
 size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p);
+
+/* Enqueue on `stream` a copy of the device status word of the ssd_combined_fwd call that
+ * used `workspace` (its first 4 bytes) to `dst` (host-pinned or device memory).  The word is
+ * 0 after a complete launch; a bounded wait inside the fused kernel that gave up (a hang
+ * that was cut short) sets it.  Pass the value, once the stream reached the copy, to
+ * ssd_status_decode.  No reference counterpart: the reference's kernels have no bounded
+ * waits (its failure handling is the Python fallback of src/mamba2_jax/modules/mamba2.py:59-74). */
+int ssd_status_copy_async(const void* workspace, uint32_t* dst, ssd_stream_t stream);
+
+/* SSD_OK for a zero status word, else the status it records (SSD_ERR_TIMEOUT for a bounded
+ * wait that gave up, SSD_ERR_ALIGNMENT for an unusable shared-memory window), with a
+ * description in ssd_last_error().  No reference counterpart (see above). */
+int ssd_status_decode(uint32_t word);
 
 /* 1 if ssd_combined_fwd runs the tcgen05 tensor-core pipeline for these params, else 0
  * (fp32 CUDA-core pipeline).  No reference counterpart: introspection for callers that

@@ -32,6 +32,10 @@ bool dtype_ok(int d) { return d == SSD_DTYPE_F32 || d == SSD_DTYPE_BF16; }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// Every workspace starts with this region: the device status word (first 4 bytes), cleared
+// on the stream by each ssd_combined_fwd call and set by a bounded wait that gives up.
+constexpr size_t STATUS_BYTES = 256;
+
 int check_dims(int64_t b, int64_t L, int64_t H, int64_t P, int64_t G, int64_t N, int64_t Q) {
   if (b <= 0 || L <= 0 || H <= 0 || P <= 0 || G <= 0 || N <= 0 || Q <= 0)
     return fail(SSD_ERR_INVALID_ARG, "dims must be positive (b=%lld L=%lld H=%lld P=%lld G=%lld N=%lld Q=%lld)",
@@ -52,7 +56,7 @@ Workspace plan_ws(const ssd_fwd_params_t* p) {
   const size_t st = (size_t)p->batch * nc * p->nheads * p->headdim * p->dstate * sizeof(float);
   const size_t cb = (size_t)p->batch * nc * p->ngroups * p->chunk_size * p->chunk_size * sizeof(float);
   Workspace w;
-  size_t off = 0;
+  size_t off = STATUS_BYTES;   // the status word leads every workspace
   w.dA = off; off += align256(cs);
   w.dt = off; off += align256(cs);
   w.states = off; off += align256(st);
@@ -122,7 +126,7 @@ Bf16Plan plan_bf16(const ssd_fwd_params_t* p, const void* workspace) {
   if (!(p->flags & SSD_FLAG_BF16_MMA) || p->dtype != SSD_DTYPE_F32 || (p->flags & SSD_FLAG_FORCE_SIMT)) return r;
   const size_t nx = (size_t)p->batch * p->seqlen * p->nheads * p->headdim;
   const size_t nb = (size_t)p->batch * p->seqlen * p->ngroups * p->dstate;
-  size_t off = 0;
+  size_t off = STATUS_BYTES;
   r.off_x = off; off += align256(nx * 2);
   r.off_b = off; off += align256(nb * 2);
   r.off_c = off; off += align256(nb * 2);
@@ -155,11 +159,37 @@ int ssd_abi_version(void) { return SSD_B200_ABI_VERSION; }
 
 size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p) {
   if (!p) return 0;
+  {
+    char keep[sizeof(g_err)];   // sizing is a query: leave the last error as it was
+    memcpy(keep, g_err, sizeof(g_err));
+    const int s = validate_fwd(p);
+    memcpy(g_err, keep, sizeof(g_err));
+    if (s) return 0;
+  }
   const Bf16Plan bp = plan_bf16(p, nullptr);
   if (bp.on) return bp.bytes + ssd::tc_workspace_bytes(&bp.q);
-  const size_t tc = ssd::tc_workspace_bytes(p);
+  const size_t tc = STATUS_BYTES + ssd::tc_workspace_bytes(p);
   const size_t simt = plan_ws(p).total;
   return tc > simt ? tc : simt;
+}
+
+int ssd_status_copy_async(const void* workspace, uint32_t* dst, ssd_stream_t stream) {
+  g_err[0] = 0;
+  if (!workspace || !dst) return fail(SSD_ERR_INVALID_ARG, "workspace and dst are required");
+  return cuda_status(cudaMemcpyAsync(dst, workspace, sizeof(uint32_t), cudaMemcpyDefault, (cudaStream_t)stream),
+                     "cudaMemcpyAsync of the status word");
+}
+
+int ssd_status_decode(uint32_t word) {
+  g_err[0] = 0;
+  if (word == 0) return SSD_OK;
+  if ((word & ~0xffu) == 0x100u)
+    return fail(SSD_ERR_TIMEOUT, "a bounded wait of the fused kernel gave up (barrier %u); the launch's outputs "
+                "are incomplete", word & 0xffu);
+  if (word == 0x200u)
+    return fail(SSD_ERR_ALIGNMENT, "the fused kernel's dynamic shared memory window was not 1024-byte alignable; "
+                "the launch did no work");
+  return fail(SSD_ERR_CUDA, "unknown device status word 0x%x", word);
 }
 
 int ssd_combined_uses_tensor_cores(const ssd_fwd_params_t* p) {
@@ -185,6 +215,9 @@ int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspac
   if (!workspace || workspace_bytes < need)
     return fail(SSD_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given", need, workspace_bytes);
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(SSD_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  unsigned* status = (unsigned*)workspace;
+  if ((s = cuda_status(cudaMemsetAsync(status, 0, sizeof(unsigned), st), "cudaMemsetAsync of the status word")))
+    return s;
 
   // fp32 inputs with bf16 MMA operands: convert, then the tensor-core pipeline
   const Bf16Plan bp = plan_bf16(p, workspace);
@@ -202,12 +235,12 @@ int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspac
     const unsigned gx = (unsigned)std::min<int64_t>((most / 4 + 255) / 256, 4 * 148);
     to_bf16_kernel<<<dim3(gx, 4), 256, 0, st>>>(j);
     if ((s = cuda_status(cudaGetLastError(), "to_bf16_kernel"))) return s;
-    return ssd::tc_combined_fwd(&bp.q, ws + bp.bytes, st);
+    return ssd::tc_combined_fwd(&bp.q, status, ws + bp.bytes, st);
   }
 
   // Tensor-core pipeline for bf16 inputs when the shape is one it covers.
   if (!(p->flags & SSD_FLAG_FORCE_SIMT) && ssd::tc_supported(p)) {
-    return ssd::tc_combined_fwd(p, workspace, st) ;
+    return ssd::tc_combined_fwd(p, status, (char*)workspace + STATUS_BYTES, st);
   }
 
   const Workspace w = plan_ws(p);

@@ -49,6 +49,9 @@ int ssd_combined_fwd_noalloc(const ssd_fwd_params_t* p, ssd_stream_t stream) {
     return SSD_ERR_INVALID_ARG;
   }
   const size_t need = ssd_combined_workspace_bytes(p);
+  // 0: the params are invalid; the workspace entry point reports why before touching
+  // any buffer
+  if (need == 0) return ssd_combined_fwd(p, nullptr, 0, stream);
   if (need > (size_t)SSD_NOALLOC_SCRATCH_BYTES) {
     snprintf(g_err_local, sizeof(g_err_local),
              "ssd_combined_fwd_noalloc: these shapes need %zu bytes of scratch, more than the %d-byte "

@@ -47,6 +47,8 @@
 #include <cstdlib>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "ptx_sm100.cuh"
 #include "ssd_kernels.h"
@@ -150,6 +152,7 @@ struct TcArgs {
   const int* sched_n;          // chunk count written by the schedule kernel, or null
   const int2* sched;           // {t0, varlen slot or -1} per chunk, entry nci = {L, -1}
   unsigned* status;
+  long long test_wait_cycles;  // > 0: test mode, see the start of ssd_fused_tc_kernel
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
@@ -281,7 +284,7 @@ __device__ void producer(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, i
 }
 
 // ---------------------------------------------------------------------------
-// dA producer (warp 2, lane 0): each chunk's dA and w arrays (from the dt pre-pass) into the
+// dA producer (warp 3, lane 0): each chunk's dA and w arrays (from the dt pre-pass) into the
 // shared arrays of its parity, as soon as the readers of chunk c-2 have released them.
 // Kept apart from the C/B/x producer so neither waits on the other's consumers.
 // ---------------------------------------------------------------------------
@@ -310,7 +313,7 @@ __device__ void da_producer(const TcArgs& a, Misc* m, int bi, int h) {
 //   A (warp 1, lane 0)  MMA1(c)  CB = C.B^T   into CB buffer c%2, after C,B(c) and E2(c-2)
 //                       MMA2(c)  Y = S.x      after the scores of c (in that CB buffer), x(c)
 //                                             and the output of c-1
-//   B (warp 3, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, a free Yi buffer
+//   B (warp 0, lane 0)  MMA3(c)  Yi = C.S_c^T after C(c), the bf16 state S_c, a free Yi buffer
 //                       MMA_L(c) S += B^T.xs  onto the state T has scaled by the chunk decay
 // With one chunk of C/B per ring stage (N=128), A issues MMA1(c+1) before MMA2(c), so the
 // scores of chunk c+1 can start as soon as those of c are done.  MMA2(c) and MMA1(c+2) share
@@ -1022,7 +1025,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   __syncthreads();
   ptx::tc_fence_after();
 
-  if (warp == W_PRODUCER) {
+  if (a.test_wait_cycles > 0) {
+    // Test mode (SSD_FLAG_TEST_WAIT_TIMEOUT): a bounded wait on a barrier that nothing
+    // arrives on yet (DRAIN, before any role has run) runs out, the status word records it
+    // and the CTA skips its work.  It exercises the timeout report with no copy or MMA in
+    // flight.
+    if (threadIdx.x == 0) {
+      const long long t0 = clock64();
+      bool ok = false;
+      while (!(ok = ptx::mbar_try_wait(&m->bar[DRAIN], 0)) && clock64() - t0 < a.test_wait_cycles) {
+      }
+      if (!ok) {
+        m->abort = 1;
+        atomicCAS(a.status, 0u, (unsigned)(0x100 | DRAIN));
+      }
+    }
+    __syncthreads();
+  }
+  if (m->abort) {
+    // nothing issued: fall through to the TMEM release
+  } else if (warp == W_PRODUCER) {
     if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
   } else if (warp == W_ISSUE_A) {
     if (lane == 0) mma_issuer_a<NT>(a, sm, m);
@@ -1221,8 +1243,9 @@ bool trace_enabled() {
   return on == 1;
 }
 
-// Workspace: 256 bytes of device status word; with varlen states the chunk schedule
-// (an 8-byte header, then cap + 1 int2 entries); with SSD_TC_TRACE=1 a 64 KB phase trace.
+// Workspace (the status word is separate, owned by the caller): with varlen states the
+// chunk schedule (an 8-byte header, then cap + 1 int2 entries); the dt pre-pass output; with
+// SSD_TC_TRACE=1 a 64 KB phase trace.
 int64_t sched_cap(const ssd_fwd_params_t* p) { return (p->seqlen + QI - 1) / QI + p->num_seqs + 2; }
 size_t sched_bytes(const ssd_fwd_params_t* p) {
   return p->varlen_states ? (size_t)(8 + 8 * (sched_cap(p) + 1) + 255) / 256 * 256 : 0;
@@ -1235,12 +1258,28 @@ int64_t prep_cap(const ssd_fwd_params_t* p) {
 size_t prep_bytes(const ssd_fwd_params_t* p) { return (size_t)p->batch * p->nheads * prep_cap(p) * 2 * QI * 4; }
 
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
-  return tc_supported(p) ? 256 + sched_bytes(p) + prep_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 + 65536 : 0) : 0;
+  return tc_supported(p) ? sched_bytes(p) + prep_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 + 65536 : 0) : 0;
 }
 
 int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : 2; }
 
-int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st) {
+// Dynamic shared memory opt-in, per device and kernel variant (the attribute belongs to the
+// current device's context, so a process that drives several GPUs sets it on each).
+bool ensure_smem_attr(void (*kern)(TcArgs), int kid) {
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static uint8_t done[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < kMaxDev && (done[dev] >> kid & 1)) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) != cudaSuccess)
+    return false;
+  if (dev >= 0 && dev < kMaxDev) done[dev] |= (uint8_t)(1u << kid);
+  return true;
+}
+
+int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace, cudaStream_t st) {
   TcArgs a;
   memset(&a, 0, sizeof(a));
   const int64_t b = p->batch, L = p->seqlen, H = p->nheads, G = p->ngroups;
@@ -1257,29 +1296,22 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
   a.x = (const bf16*)p->x; a.z = (const bf16*)p->z; a.init = p->initial_states; a.seq_idx = p->seq_idx;
   a.out = p->out; a.out_x = p->z ? p->out_x : nullptr; a.final_states = p->final_states;
   a.varlen_states = p->varlen_states;
-  a.status = (unsigned*)workspace;
-  float* prep_out = (float*)((char*)workspace + 256 + sched_bytes(p));
+  a.status = status;
+  a.test_wait_cycles = (p->flags & SSD_FLAG_TEST_WAIT_TIMEOUT) ? 20000 : 0;
+  float* prep_out = (float*)((char*)workspace + sched_bytes(p));
   a.dtprep = prep_out;
   a.prep_cap = (int)prep_cap(p);
-  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + 256 + sched_bytes(p) + prep_bytes(p)) : nullptr;
+  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + sched_bytes(p) + prep_bytes(p)) : nullptr;
   typedef void (*KernelFn)(TcArgs);
   static const KernelFn kernels[8] = {
       ssd_fused_tc_kernel<128, false, false>, ssd_fused_tc_kernel<128, false, true>,
       ssd_fused_tc_kernel<128, true, false>,  ssd_fused_tc_kernel<128, true, true>,
       ssd_fused_tc_kernel<256, false, false>, ssd_fused_tc_kernel<256, false, true>,
       ssd_fused_tc_kernel<256, true, false>,  ssd_fused_tc_kernel<256, true, true>};
-  static bool attr[8] = {false, false, false, false, false, false, false, false};
   const int kid = (p->dstate == 256 ? 4 : 0) + (p->seq_idx ? 2 : 0) + (p->z ? 1 : 0);
   const KernelFn kern = kernels[kid];
-  if (!attr[kid]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) != cudaSuccess) {
-      set_last_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
-      return SSD_ERR_CUDA;
-    }
-    attr[kid] = true;
-  }
-  if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) {
-    set_last_error("cudaMemsetAsync of the status word failed");
+  if (!ensure_smem_attr(kern, kid)) {
+    set_last_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
     return SSD_ERR_CUDA;
   }
   if (p->varlen_states) {
@@ -1288,8 +1320,8 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st)
       set_last_error("varlen chunk schedule too long");
       return SSD_ERR_UNSUPPORTED;
     }
-    int* hdr = (int*)((char*)workspace + 256);
-    int2* sched = (int2*)((char*)workspace + 264);
+    int* hdr = (int*)workspace;
+    int2* sched = (int2*)((char*)workspace + 8);
     tc_schedule_kernel<<<1, SCHED_THREADS, 0, st>>>(p->cu_seqlens, p->num_seqs, (int)L, (int)cap, hdr, sched,
                                                     p->varlen_states, H * PT * p->dstate);
     a.sched_n = hdr;

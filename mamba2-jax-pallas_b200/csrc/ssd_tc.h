@@ -9,11 +9,12 @@ namespace ssd {
 
 // True when the tcgen05 pipeline covers these params (bf16 inputs, supported shape).
 bool tc_supported(const ssd_fwd_params_t* p);
-// Workspace bytes the tcgen05 pipeline needs (0 when unsupported).
+// Workspace bytes the tcgen05 pipeline needs besides the status word (0 when unsupported).
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p);
 // Kernel launches one tc_combined_fwd call enqueues.
 int tc_num_launches(const ssd_fwd_params_t* p);
-// Enqueue the tcgen05 pipeline.  Requires tc_supported(p).
-int tc_combined_fwd(const ssd_fwd_params_t* p, void* workspace, cudaStream_t st);
+// Enqueue the tcgen05 pipeline.  Requires tc_supported(p).  `status` is the device status
+// word (cleared by the caller on the stream); a bounded wait that gives up writes there.
+int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace, cudaStream_t st);
 
 }  // namespace ssd

@@ -22,6 +22,9 @@ SSD_DTYPE_BF16 = 1
 SSD_FLAG_FORCE_SIMT = 1
 SSD_FLAG_ROUND_STATES = 2
 SSD_FLAG_BF16_MMA = 4
+SSD_FLAG_TEST_WAIT_TIMEOUT = 8
+# the ssd_b200.h these ctypes structures describe
+ABI_VERSION = 2
 SSD_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 STATUS_NAMES = {0: "SSD_OK", 1: "SSD_ERR_INVALID_ARG", 2: "SSD_ERR_UNSUPPORTED",
@@ -33,7 +36,8 @@ EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
             "ssd_combined_num_launches", "ssd_combined_fwd", "ssd_combined_fwd_noalloc", "ssd_chunk_cumsum_fwd",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
-            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_sp_state_fixup", "ssd_last_error", "ssd_abi_version"]
+            "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_sp_state_fixup", "ssd_status_copy_async", "ssd_status_decode",
+            "ssd_last_error", "ssd_abi_version"]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -142,11 +146,14 @@ def load() -> ctypes.CDLL:
     lib.ssd_chunk_state_varlen_fwd.argtypes = [_vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _i32,
                                                _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]
     lib.ssd_selective_state_update.argtypes = [P(SsuParams), _vp]
+    lib.ssd_status_copy_async.argtypes = [_vp, _vp, _vp]
+    lib.ssd_status_decode.argtypes = [ctypes.c_uint32]
     for name in EXPORTED:
         if name not in ("ssd_last_error", "ssd_abi_version", "ssd_combined_workspace_bytes"):
             getattr(lib, name).restype = ctypes.c_int
-    if lib.ssd_abi_version() != 1:
-        raise RuntimeError("libssd_b200.so ABI version mismatch")
+    if lib.ssd_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"libssd_b200.so has ABI version {lib.ssd_abi_version()}, these bindings "
+                           f"describe version {ABI_VERSION}: rebuild the library")
     _lib = lib
     return lib
 
@@ -155,6 +162,17 @@ def check(code: int) -> None:
     if code != 0:
         msg = load().ssd_last_error().decode(errors="replace")
         raise SsdError(code, msg)
+
+
+def check_device_status(workspace: torch.Tensor, stream=None) -> None:
+    """Read the device status word of the last ssd_combined_fwd call that used ``workspace``
+    (waits for that stream) and raise SsdError if a bounded wait inside the kernel gave up."""
+    lib = load()
+    s = torch.cuda.current_stream(workspace.device) if stream is None else stream
+    word = torch.empty(1, dtype=torch.int32, device=workspace.device)
+    check(lib.ssd_status_copy_async(workspace.data_ptr(), word.data_ptr(), s.cuda_stream))
+    s.synchronize()
+    check(lib.ssd_status_decode(int(word.item()) & 0xFFFFFFFF))
 
 
 # ---------------------------------------------------------------------------

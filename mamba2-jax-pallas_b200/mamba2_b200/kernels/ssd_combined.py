@@ -66,6 +66,7 @@ def mamba_chunk_scan_combined_fwd(
     dt_limit: tuple = (0.0, float("inf")), return_final_states: bool = False,
     return_varlen_states: bool = False, *, round_states: bool = False,
     force_simt: bool = False, bf16_mma: bool = False, return_out_x: bool = False, workspace=None,
+    check_status: bool = False,
 ):
     """Mamba2 SSD chunked-scan forward (reference ``ssd_combined.py:46-203``).
 
@@ -76,7 +77,9 @@ def mamba_chunk_scan_combined_fwd(
     ``force_simt`` selects the fp32 CUDA-core pipeline; ``bf16_mma`` runs fp32 inputs on the
     tensor-core pipeline with bf16 MMA operands (the reference's Pallas kernels do the same
     for fp32 inputs), instead of exact fp32 on the CUDA cores; ``return_out_x`` appends the
-    pre-gate output; ``workspace`` is an optional preallocated uint8 CUDA tensor.
+    pre-gate output; ``workspace`` is an optional preallocated uint8 CUDA tensor;
+    ``check_status`` waits for the call and raises ``SsdError`` (SSD_ERR_TIMEOUT) if a bounded
+    wait inside the fused kernel gave up (the default leaves the call asynchronous).
     """
     if not return_varlen_states:
         cu_seqlens = None
@@ -109,6 +112,8 @@ def mamba_chunk_scan_combined_fwd(
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(max(nbytes, 1), device=dev, dtype=torch.uint8)
     _lib.check(lib.ssd_combined_fwd(p, workspace.data_ptr(), workspace.numel(), _lib.stream_of(out)))
+    if check_status:
+        _lib.check_device_status(workspace)
     res = [out]
     if return_final_states:
         res.append(final)

@@ -97,19 +97,21 @@ def combine(a1, s1, a2, s2):
     return a1 * a2, a2[..., None, None] * s1 + s2
 
 
-def exclusive_prefix(decay: torch.Tensor, state: torch.Tensor, group=None):
+def exclusive_prefix(decay: torch.Tensor, state: torch.Tensor, group=None, timeout=None):
     """Exclusive scan of (decay, state) pairs over the ranks of `group` in rank order.
 
     Recursive doubling: in round k every rank sends its inclusive partial to rank+2^k and
     receives from rank-2^k.  Returns the combination of all lower ranks' pairs (decay 1 and
     state 0 on rank 0).  Works on the gloo (CPU tensors) and NCCL (CUDA tensors) backends.
+    ``timeout`` (a ``datetime.timedelta``) bounds each round's wait: a peer that died or
+    stalls makes this rank raise instead of waiting for the process group's own timeout.
     """
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     if decay.is_cuda and dist.get_backend(group) == "gloo":
         # gloo moves host tensors only: stage through host memory (tests of the path on one GPU)
-        a, s = exclusive_prefix(decay.cpu(), state.cpu(), group)
+        a, s = exclusive_prefix(decay.cpu(), state.cpu(), group, timeout)
         return a.to(decay.device), s.to(state.device)
     inc_a, inc_s = decay.clone(), state.clone()          # inclusive partial of this rank
     exc_a, exc_s = torch.ones_like(decay), torch.zeros_like(state)
@@ -125,7 +127,10 @@ def exclusive_prefix(decay: torch.Tensor, state: torch.Tensor, group=None):
                     dist.P2POp(dist.irecv, rs, _peer(rank - k, group), group)]
         if ops:
             for req in dist.batch_isend_irecv(ops):
-                req.wait()
+                if timeout is None:
+                    req.wait()
+                elif not req.wait(timeout):
+                    raise RuntimeError(f"exclusive_prefix: round {k} did not complete within {timeout}")
         if rank - k >= 0:
             # the received partial covers ranks just below this one's current span
             exc_a, exc_s = combine(ra, rs, exc_a, exc_s)

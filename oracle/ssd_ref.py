@@ -5,16 +5,18 @@ TEST INFRASTRUCTURE ONLY.  This module is the checker for the CUDA path: only
 arm may import it.  The product path (``mamba2_b200``) never calls it and has no
 CPU fallback.
 
-Parity status: the reference (JAX + Pallas Mosaic) cannot be imported in this
-environment (jax/jaxlib are not installed and there is no wheel), and it ships no
-golden vectors or fixtures.  This restatement is therefore pinned against the
-reference's own known-answer *procedures* (decode-step hand formula of
-``tests/test_mamba2_ops.py:25-112``; the sequential state-passing loop of
-``tests/test_state_passing_and_bmm.py:92-138``; the per-sequence varlen loop of
-``tests/test_chunk_scan_and_varlen.py:504-589``) restated here and cross-checked
-against the vectorised ``ssd_naive`` form, plus size-independent properties
-(packed == per-sequence, prefill == decode loop, split-resume == full).  Against
-the reference's actual outputs, parity is **unpinned**.
+Parity status: pinned to the reference's own outputs.  JAX cannot be installed in this
+environment, so ``tests/golden/make_fixtures.py`` runs the reference's unmodified
+``ops/ssd_naive.py``, ``ops/selective_state_update.py``, ``ops/rms_norm.py`` and
+``ops/causal_conv1d.py`` on a NumPy stand-in for ``jax`` (``tests/golden/jaxshim``) and
+commits the results as fixtures; ``tests/test_golden.py`` checks this module against them
+(rel-L2 <= 1e-6 against the reference's float64 run, 2e-5 against its float32 run).  The
+seq_idx rules, which ``ssd_naive`` does not implement, are pinned through per-sequence
+reference runs of a packed row and by restating the reference's known-answer procedures
+(decode-step hand formula of ``tests/test_mamba2_ops.py:25-112``; the sequential
+state-passing loop of ``tests/test_state_passing_and_bmm.py:92-138``; the per-sequence
+varlen loop of ``tests/test_chunk_scan_and_varlen.py:504-589``), plus size-independent
+properties (packed == per-sequence, prefill == decode loop, split-resume == full).
 
 Every array is float64 unless noted.  Shapes follow the reference:
 x (b,L,H,P), dt (b,L,H), A (H,), B/C (b,L,G,N), D (H,) or (H,P), z (b,L,H,P),

@@ -30,7 +30,7 @@ def test_header_symbols_exported():
 
 
 def test_abi_version():
-    assert _lib.load().ssd_abi_version() == 1
+    assert _lib.load().ssd_abi_version() == _lib.ABI_VERSION == 2
 
 
 def _params(**kw):
@@ -97,3 +97,45 @@ def test_python_api_refuses_cpu_tensors():
         mamba_chunk_scan_combined_fwd(x, dt, A, B, B, 64)
     with pytest.raises(ValueError, match="CUDA"):
         selective_state_update(torch.zeros(1, 2, 8, 16), x[:, 0], dt[:, 0], A, B[:, 0], B[:, 0])
+
+
+@pytest.mark.parametrize("kw", [dict(chunk_size=0), dict(batch=-1), dict(seqlen=-5), dict(nheads=0),
+                                dict(dstate=-128)])
+def test_invalid_dims_rejected_before_sizing(kw):
+    """Sizing returns 0 for invalid params (no division by a zero chunk size), and both
+    entry points report SSD_ERR_INVALID_ARG without touching a device."""
+    lib = _lib.load()
+    p = _params(**kw)
+    assert lib.ssd_combined_workspace_bytes(p) == 0
+    assert lib.ssd_combined_fwd_noalloc(p, None) == 1
+    assert b"positive" in lib.ssd_last_error()
+    assert lib.ssd_combined_fwd(p, 256, 1 << 40, None) == 1
+
+
+def test_status_decode():
+    lib = _lib.load()
+    assert lib.ssd_status_decode(0) == 0
+    assert lib.ssd_status_decode(0x100 | 7) == 6          # SSD_ERR_TIMEOUT
+    assert b"bounded wait" in lib.ssd_last_error()
+    assert lib.ssd_status_decode(0x200) == 3              # SSD_ERR_ALIGNMENT
+    assert lib.ssd_status_decode(0xdead) == 5
+    assert lib.ssd_status_copy_async(None, 4096, None) == 1
+
+
+def test_dispatch_is_the_reference_keyword_call():
+    """mamba2_b200.dispatch._ssd_combined_fwd takes the reference module's keyword-only call
+    (src/mamba2_jax/modules/mamba2.py:377-389) and has no fallback: CPU tensors raise."""
+    import inspect
+    from mamba2_b200 import dispatch
+    from mamba2_b200.kernels.ssd_combined import mamba_chunk_scan_combined_fwd
+    params = inspect.signature(mamba_chunk_scan_combined_fwd).parameters
+    for k in ("x", "dt", "A", "B", "C", "chunk_size", "D", "z", "dt_bias", "initial_states", "seq_idx",
+              "cu_seqlens", "dt_softplus", "dt_limit", "return_final_states", "return_varlen_states"):
+        assert k in params, k
+    x = torch.zeros(1, 64, 2, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        dispatch._ssd_combined_fwd(use_pallas=True, x=x, dt=torch.zeros(1, 64, 2), A=-torch.ones(2),
+                                   B=torch.zeros(1, 64, 1, 16), C=torch.zeros(1, 64, 1, 16), chunk_size=64,
+                                   D=torch.ones(2), z=None, dt_bias=torch.zeros(2), initial_states=None,
+                                   seq_idx=None, dt_softplus=True, dt_limit=(0.0, float("inf")),
+                                   return_final_states=True)

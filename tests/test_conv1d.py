@@ -203,3 +203,86 @@ def test_conv1d_layer_shape_full_size():
     ref = R.causal_conv1d(xbc.transpose(1, 2)[:, sl].double().cpu().numpy(), w[sl].double().cpu().numpy(),
                           bias[sl].double().cpu().numpy(), activation="silu")
     np.testing.assert_allclose(out[:, sl].double().cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+def _cl_tensor(xs, dtype, layout):
+    b, d, L = xs.shape
+    if layout == "channels-last":
+        return torch.from_numpy(xs.transpose(0, 2, 1).copy()).to(dtype).cuda().transpose(1, 2)
+    if layout == "contiguous":
+        return torch.from_numpy(xs).to(dtype).cuda()
+    big = torch.zeros((b, 2 * d, L + 3), dtype=dtype, device="cuda")
+    big[:, ::2, 3:] = torch.from_numpy(xs).to(dtype).cuda()
+    return big[:, ::2, 3:]
+
+
+_TD = {"f32": torch.float32, "bf16": torch.bfloat16}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+@pytest.mark.parametrize("wdt", ["f32", "bf16"])
+@pytest.mark.parametrize("bdt", ["f32", "bf16", None])
+@pytest.mark.parametrize("width", [3, 4])
+def test_conv1d_capi_independent_param_dtypes(layout, xdt, wdt, bdt, width):
+    """The C ABI takes weight and bias in f32 or bf16 independently of x (converted on load):
+    every combination, in the three layouts, against the oracle on the same (bf16-representable)
+    values.  width 3 with f32 x puts the channels-last kernel's 8-byte weight loads at 24-byte
+    offsets."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    rng = np.random.default_rng(17 * width + len(layout))
+    b, d, L = 2, 96, 150
+    xs = _round(rng.standard_normal((b, d, L)), torch.bfloat16)
+    w = _round(rng.standard_normal((d, width)) * 0.5, torch.bfloat16)
+    bs = _round(rng.standard_normal(d), torch.bfloat16)
+    sq = _seq(b, L, rng)
+    xt = _cl_tensor(xs, _TD[xdt], layout)
+    wt = torch.from_numpy(w).to(_TD[wdt]).cuda().contiguous()
+    bt = None if bdt is None else torch.from_numpy(bs).to(_TD[bdt]).cuda()
+    st = torch.from_numpy(sq).cuda()
+    out = torch.empty((b, L, d), device="cuda").transpose(1, 2)
+    p = _lib.Conv1dParams(batch=b, dim=d, seqlen=L, x_stride_b=xt.stride(0), x_stride_d=xt.stride(1),
+                          x_stride_t=xt.stride(2), out_stride_b=out.stride(0), out_stride_d=out.stride(1),
+                          out_stride_t=out.stride(2), width=width, dtype=_lib.dtype_code(xt),
+                          out_dtype=0, silu=1)
+    p.x, p.weight, p.bias, p.seq_idx, p.out = xt.data_ptr(), wt.data_ptr(), _lib.ptr(bt), st.data_ptr(), out.data_ptr()
+    p.weight_dtype = _lib.dtype_code(wt)
+    p.bias_dtype = 0 if bt is None else _lib.dtype_code(bt)
+    _lib.check(_lib.load().ssd_causal_conv1d_fwd(p, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    ref = R.causal_conv1d(xs, w, None if bdt is None else bs, activation="silu", seq_idx=sq)
+    np.testing.assert_allclose(out.double().cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("wdt,bdt", [("bf16", "bf16"), ("bf16", "f32"), ("f32", "bf16")])
+def test_conv1d_update_capi_param_dtypes(wdt, bdt):
+    """Decode steps with an f32 state and bf16 x through the C ABI, weight and bias dtypes
+    chosen independently, against the oracle's decode loop."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    rng = np.random.default_rng(3)
+    b, d, k, steps = 3, 200, 4, 6
+    w = _round(rng.standard_normal((d, k)) * 0.5, torch.bfloat16)
+    bs = _round(rng.standard_normal(d), torch.bfloat16)
+    xs = _round(rng.standard_normal((steps, b, d)), torch.bfloat16)
+    wt = torch.from_numpy(w).to(_TD[wdt]).cuda()
+    bt = torch.from_numpy(bs).to(_TD[bdt]).cuda()
+    state = torch.zeros((b, d, k), device="cuda")
+    ref_state = np.zeros((b, d, k))
+    lib = _lib.load()
+    for t in range(steps):
+        xt = torch.from_numpy(xs[t]).to(torch.bfloat16).cuda()
+        out = torch.empty((b, d), device="cuda")
+        p = _lib.Conv1dUpdateParams(batch=b, dim=d, state_stride_b=state.stride(0), state_stride_d=state.stride(1),
+                                    width=k, x_dtype=1, state_dtype=0, out_dtype=0, silu=1)
+        p.x_new, p.conv_state, p.weight, p.bias, p.out = (xt.data_ptr(), state.data_ptr(), wt.data_ptr(),
+                                                          bt.data_ptr(), out.data_ptr())
+        p.weight_dtype, p.bias_dtype = _lib.dtype_code(wt), _lib.dtype_code(bt)
+        _lib.check(lib.ssd_causal_conv1d_update(p, torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        ref_state, ref_o = R.causal_conv1d_update(xs[t], ref_state, w, bs, activation="silu")
+        np.testing.assert_allclose(state.double().cpu().numpy(), ref_state, rtol=0, atol=0)
+        np.testing.assert_allclose(out.double().cpu().numpy(), ref_o, rtol=1e-5, atol=1e-5)

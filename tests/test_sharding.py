@@ -119,6 +119,54 @@ def test_exclusive_prefix_gloo(world):
         acc_a, acc_s = SH.combine(acc_a, acc_s, *_pair(r))
 
 
+def _failing_prefix_worker(rank, world, port, q):
+    """Rank 1 dies before the exchange; the others run it with a 5 s bound per round."""
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    if rank == 1:
+        os._exit(3)
+    a, s = _pair(rank)
+    try:
+        SH.exclusive_prefix(a, s, timeout=datetime.timedelta(seconds=5))
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001 - the failure is the point
+        q.put((rank, f"error: {type(e).__name__}"))
+    q.close()
+    q.join_thread()      # flush the message before the hard exit
+    os._exit(0)
+
+
+def test_exclusive_prefix_peer_failure_is_detected():
+    """A rank that exits instead of joining the exchange makes the rank that needs its
+    partial (rank 2 receives from rank 1 in the first round) raise within the bound, with no
+    hang; rank 0, which receives nothing, may finish."""
+    import time
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_failing_prefix_worker, args=(r, world, port, q)) for r in range(world)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world - 1):
+            r, msg = q.get(timeout=120)
+            res[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert procs[1].exitcode == 3
+    assert res[2].startswith("error"), res
+    assert time.time() - t0 < 110
+
+
 # ---------------------------------------------------------------------------
 # the algorithm against the oracle (float64)
 # ---------------------------------------------------------------------------
