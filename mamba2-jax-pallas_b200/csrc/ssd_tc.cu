@@ -49,6 +49,7 @@
 #include <cstdlib>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -132,7 +133,8 @@ constexpr uint32_t DA_FREE_COUNT = 16;        // SA, SB, T and O warps done with
 struct Misc {
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
   // Per token t of 32-token block k: w_t = exp(dA_{32k} - dA_t) dt_t when block k is
-  // factored (block_factored), else the processed dt_t.
+  // factored as a whole (block_factored), w_t = exp(dA_{8j} - dA_t) dt_t for its 8-token
+  // sub-block j when factored by sub-block (block_factored8), else the processed dt_t.
   float dt[2][QI];
   float Dh;             // skip coefficient of the head (0 without D)
   uint64_t bar[NBARS];
@@ -165,6 +167,7 @@ struct TcArgs {
   const int2* sched;           // {t0, varlen slot or -1} per chunk, entry nci = {L, -1}
   unsigned* status;
   long long test_wait_cycles;  // > 0: test mode, see the start of ssd_fused_tc_kernel
+  int seg_k;                   // rows per batch row when the sequence is split (1: no split)
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
@@ -528,6 +531,26 @@ __device__ __forceinline__ bool block_factored(bool factor, const float* dA, int
   return factor && (dA[32 * k] - dA[32 * k + 31] <= FAC_RANGE);
 }
 
+// The reference point of row r's decay factor w_r in the dt pre-pass output (the start of its
+// 32-token block, of its 8-token sub-block, or r itself): exp(dA_x - dA_r) dt_r =
+// exp(dA_x - ref) w_r for any x.
+__device__ __forceinline__ bool block_factored8(bool factor, const float* dA, int k);
+__device__ __forceinline__ float w_ref(bool factor, const float* dA, int r) {
+  const int q = r >> 5;
+  if (block_factored(factor, dA, q)) return dA[32 * q];
+  if (block_factored8(factor, dA, q)) return dA[r & ~7];
+  return dA[r];
+}
+
+// Blocks that do not factor as a whole may still factor by 8-token sub-block (heads whose dA
+// falls by more than 60 over 32 tokens but by at most 60 over every 8).  The dt pre-pass and
+// the consumers decide it from the same dA values.
+__device__ __forceinline__ bool block_factored8(bool factor, const float* dA, int k) {
+  const float* d = dA + 32 * k;
+  return factor && d[0] - d[7] <= FAC_RANGE && d[8] - d[15] <= FAC_RANGE && d[16] - d[23] <= FAC_RANGE &&
+         d[24] - d[31] <= FAC_RANGE;
+}
+
 template <bool DT_BF16>
 __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__ TcArgs a, float* __restrict__ out) {
   const int c = blockIdx.x, bi = blockIdx.y;
@@ -558,9 +581,16 @@ __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__
   const float dAs = __shfl_sync(0xffffffffu, dAv[0], lane & ~7);
   const float dAe = __shfl_sync(0xffffffffu, dAv[3], lane | 7);
   const bool fk = factor && (dAs - dAe <= FAC_RANGE);
+  // 8-token sub-blocks (lane pairs) for blocks that do not factor as a whole
+  const float dAs8 = __shfl_sync(0xffffffffu, dAv[0], lane & ~1);
+  const float dAe8 = __shfl_sync(0xffffffffu, dAv[3], lane | 1);
+  int ok8 = (dAs8 - dAe8 <= FAC_RANGE) ? 1 : 0;
+  ok8 &= __shfl_xor_sync(0xffffffffu, ok8, 2);
+  ok8 &= __shfl_xor_sync(0xffffffffu, ok8, 4);
+  const bool fk8 = factor && !fk && ok8;
   float w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = fk ? __expf(dAs - dAv[i]) * d[i] : d[i];
+  for (int i = 0; i < 4; ++i) w[i] = fk ? __expf(dAs - dAv[i]) * d[i] : fk8 ? __expf(dAs8 - dAv[i]) * d[i] : d[i];
   float* o = out + (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
   reinterpret_cast<float4*>(o)[lane] = make_float4(dAv[0], dAv[1], dAv[2], dAv[3]);
   reinterpret_cast<float4*>(o + QI)[lane] = make_float4(w[0], w[1], w[2], w[3]);
@@ -713,8 +743,33 @@ __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (
   }
 }
 
-// Blocks that do not factor (dA may increase, or its range in the block exceeds 60, as for
-// heads with large |A| dt): exp(dA_r - dA_t) dt_t per element.
+// Blocks factored by 8-token sub-block: decay exp(dA_r - dA_{8j}) * w_t for columns of
+// sub-block j (four exponentials per row instead of 32), masked as score_block_fac.
+template <bool HAS_SEQ>
+__device__ __noinline__ void score_block_fac8(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
+                                              const float* wc, int lim, int sl, int seqv, int dcol, float dg) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float u = __expf(dA - dAc[8 * j]);
+#pragma unroll
+    for (int i = 8 * j; i < 8 * j + 8; i += 2) {
+      float o[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        bool ok = i + e <= lim;
+        if (HAS_SEQ) {
+          const int st = __shfl_sync(0xffffffffu, sl, i + e);   // all lanes shuffle, then combine
+          ok = ok && (st == seqv);
+        }
+        o[e] = (ok ? v[i + e] * (u * wc[i + e]) : 0.f) + (i + e == dcol ? dg : 0.f);
+      }
+      pk[i / 2] = pack_bf16(o[0], o[1]);
+    }
+  }
+}
+
+// Blocks that do not factor (dA may increase, or its range within 8 tokens exceeds 60):
+// exp(dA_r - dA_t) dt_t per element.
 template <bool HAS_SEQ>
 __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
                                                   const float* dtc, int lim, int sl, int seqv, int dcol, float dg) {
@@ -796,6 +851,8 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         const int dcol = k32 == q ? lane : -1;
         if (fac && !HAS_SEQ && k32 < q) score_block_full(v, pk, __expf(dA - dAc[0]), wc);
         else if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv, dcol, dg);
+        else if (block_factored8(factor, m->dA[buf], k32))
+          score_block_fac8<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         ptx::tmem_st16(tS, pk);
         if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
@@ -849,8 +906,7 @@ __device__ __forceinline__ bool chunk_factors(const TcArgs& a, Misc* m, int bi, 
   if (!wait_barw(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return false;
   const float* dA = m->dA[buf];
   const float dA_last = dA[QI - 1];
-  const bool fq = block_factored(factor, dA, q);
-  const float e1 = __expf(dA_last - (fq ? dA[32 * q] : dA[r])) * m->dt[buf][r];
+  const float e1 = __expf(dA_last - w_ref(factor, dA, r)) * m->dt[buf][r];
   xscale = (end_seq >= 0 && seqv == end_seq) ? e1 : 0.f;
   __syncwarp();
   if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
@@ -891,6 +947,10 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
   uint8_t* st_sm = sm + G_::OFF_ST;
   const int64_t bh = (int64_t)bi * a.H + h;
+  // with a split sequence, row bi is segment bi % seg_k of batch row bi / seg_k: only the
+  // last segment's state is a final state
+  const int64_t fbh = (int64_t)(bi / a.seg_k) * a.H + h;
+  float* const fin = (bi % a.seg_k == a.seg_k - 1) ? a.final_states : nullptr;
   const int nci = m->nci;
   if (nci <= 0) return;
   const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
@@ -964,9 +1024,9 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
           sv[i + 1] = d2.y;
         }
         ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
-      } else if (a.final_states) {
+      } else if (fin) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a.final_states[(bh * PT + 32 * half + i) * NT + n] = sv[i];
+        for (int i = 0; i < 32; ++i) fin[(fbh * PT + 32 * half + i) * NT + n] = sv[i];
       }
     }
     if (more) {
@@ -1243,6 +1303,191 @@ __global__ void __launch_bounds__(SCHED_THREADS) tc_schedule_kernel(const int32_
 }
 
 // ---------------------------------------------------------------------------
+// Sequence split (few heads per GPU, e.g. one head-sharded rank of a layer).  The fused
+// kernel walks one head's chunks serially, so b*H CTAs well below the SM count leave most of
+// the GPU idle.  The sequence of each batch row is then cut into seg_k chunk-aligned
+// segments, run as seg_k rows of a (b*seg_k, L/seg_k) view of the same memory.  Segment j
+// needs the state S_j entering it:
+//   tc_segstate_kernel  per (row, head) of every segment but the last: the segment's state
+//                       from a zero start, L_j = sum_t exp(dA_end - dA_t) dt_t B_t^T x_t
+//                       (one tcgen05 accumulation over the segment's tokens; each token's
+//                       x row is scaled in shared memory), and its total dA
+//   tc_segcombine_kernel S_0 = initial state, S_{j+1} = exp(total dA_j) S_j + L_j
+// and the fused kernel then runs every segment from its S_j.  Only the state recurrence
+// crosses segments (state_passing_fwd.py:108-151 restated over segments), so outputs and
+// the final state equal the unsplit walk up to rounding.
+// ---------------------------------------------------------------------------
+struct SegArgs {
+  CUtensorMap tm_x, tm_b;
+  int H, G, k, nc;              // heads, groups, segments per row, chunks per segment
+  int rows;                     // b * k
+  float lo;                     // dt clamp minimum (the decays factor when it is >= 0)
+  const float* A;
+  const float* dtprep;          // pre-pass output of the (b*k, L/k) view
+  float* seg_state;             // (b*k, H, P, N): L_j
+  float* seg_tot;               // (b*k, H): total dA of segment j
+  unsigned* status;
+};
+
+constexpr int SEG_STAGES = 2;
+
+template <int NT>
+struct SegGeo {
+  static constexpr uint32_t SZ_B = QI * NT * 2;         // B tile of one chunk
+  static constexpr uint32_t SZ_X = QI * PT * 2;         // x tile
+  static constexpr uint32_t SZ_STAGE = SZ_B + SZ_X;
+  static constexpr uint32_t OFF_XS = SEG_STAGES * SZ_STAGE;   // two xs buffers
+  static constexpr uint32_t BYTES = OFF_XS + 2 * SZ_X;
+  static constexpr uint32_t TCOLS = NT == 256 ? 128 : 64;
+};
+
+__device__ __forceinline__ bool seg_wait(uint64_t* bar, uint32_t parity, unsigned* status, int id) {
+  const long long t0 = clock64();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > TIMEOUT_CYCLES) {
+      atomicCAS(status, 0u, (unsigned)(0x100 | id));
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_constant__ SegArgs a) {
+  using G_ = SegGeo<NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ uint64_t full[SEG_STAGES], done[2], fin;
+  __shared__ uint32_t tbase;
+  __shared__ float tots[64];
+  __shared__ volatile int bad;
+  const int r = threadIdx.x, warp = r >> 5;
+  // block -> (batch row, segment j < k-1, head)
+  const int per = (a.k - 1) * a.H;
+  const int b0 = blockIdx.x / per, rem = blockIdx.x % per;
+  const int j = rem / a.H, h = rem % a.H;
+  const int row = b0 * a.k + j, g = h / (a.H / a.G);
+  const int nc = a.nc;
+  const float* prep = a.dtprep + ((int64_t)row * a.H + h) * nc * (2 * QI);
+  if (r == 0) {
+    for (int i = 0; i < SEG_STAGES; ++i) ptx::mbar_init(&full[i], 1);
+    ptx::mbar_init(&done[0], 1);
+    ptx::mbar_init(&done[1], 1);
+    ptx::mbar_init(&fin, 1);
+    bad = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(&tbase, G_::TCOLS);
+    ptx::tmem_relinquish();
+  }
+  // chunk totals of the segment (dA of each chunk's last token), for the suffix decays
+  for (int c = r; c < nc; c += 128) tots[c] = prep[(int64_t)c * 2 * QI + QI - 1];
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (r == 0) {
+    for (int c = 0; c < nc && c < SEG_STAGES; ++c) {
+      uint8_t* st = sm + c * G_::SZ_STAGE;
+      ptx::mbar_arrive_expect_tx(&full[c], G_::SZ_STAGE);
+      for (int hh = 0; hh < NT / 64; ++hh) ptx::tma_load_3d(st + hh * (QI * 128), &a.tm_b, &full[c], g * NT + 64 * hh, c * QI, row);
+      ptx::tma_load_3d(st + G_::SZ_B, &a.tm_x, &full[c], h * PT, c * QI, row);
+    }
+  }
+  const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);
+  float suffix = 0.f;
+  for (int c = 0; c < nc; ++c) suffix += tots[c];   // total dA of the segment
+  const float total = suffix;
+  constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
+  for (int c = 0; c < nc; ++c) {
+    suffix -= tots[c];                               // dA of the chunks after c
+    const int s = c % SEG_STAGES;
+    // xs(c): row r of x scaled by exp(dA_end - dA_r) dt_r, into buffer c % 2 once MMA(c-2) is done
+    const float* dA = prep + (int64_t)c * 2 * QI;
+    const float scale = __expf(suffix + dA[QI - 1] - w_ref(factor, dA, r)) * dA[QI + r];
+    if (c >= 2 && !seg_wait(&done[c & 1], ((c >> 1) - 1) & 1, a.status, 1)) bad = 1;
+    if (!seg_wait(&full[s], (c / SEG_STAGES) & 1, a.status, 2)) bad = 1;
+    __syncthreads();   // every thread sees the same `bad` (waits above are bounded)
+    if (bad) break;
+    const uint8_t* xt = sm + s * G_::SZ_STAGE + G_::SZ_B;
+    uint8_t* xs = sm + G_::OFF_XS + (c & 1) * G_::SZ_X;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<uint4*>(xs + ptx::sw128_off(r, k)) = scale_row16(*reinterpret_cast<const uint4*>(xt + ptx::sw128_off(r, k)), scale);
+    ptx::fence_proxy_async_smem();
+    __syncthreads();
+    if (r == 0) {
+      ptx::tc_fence_after();
+      const uint32_t base = ptx::smem_u32(sm);
+      for (int hh = 0; hh < NT / 128; ++hh) {
+        const uint32_t sB = base + s * G_::SZ_STAGE + hh * (QI * 256);
+#pragma unroll
+        for (int i = 0; i < QI / 16; ++i)
+          ptx::mma_f16(tbase + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, QI * 128, 1024),
+                       ptx::sdesc_sw128(base + G_::OFF_XS + (c & 1) * G_::SZ_X + i * 2048, 8192, 1024), ID_L,
+                       (c > 0 || i > 0) ? 1u : 0u);
+      }
+      ptx::mma_commit(&done[c & 1]);
+      // refill this stage with chunk c + SEG_STAGES once MMA(c) has read it
+      if (c + SEG_STAGES < nc) {
+        if (!seg_wait(&done[c & 1], (c >> 1) & 1, a.status, 3)) {
+          bad = 1;
+        } else {
+          uint8_t* st = sm + s * G_::SZ_STAGE;
+          const int cn = c + SEG_STAGES;
+          ptx::mbar_arrive_expect_tx(&full[s], G_::SZ_STAGE);
+          for (int hh = 0; hh < NT / 64; ++hh)
+            ptx::tma_load_3d(st + hh * (QI * 128), &a.tm_b, &full[s], g * NT + 64 * hh, cn * QI, row);
+          ptx::tma_load_3d(st + G_::SZ_B, &a.tm_x, &full[s], h * PT, cn * QI, row);
+        }
+      }
+    }
+  }
+  if (r == 0) ptx::mma_commit(&fin);
+  const bool ok = seg_wait(&fin, 0, a.status, 4) && !bad;
+  ptx::tc_fence_after();
+  if (ok) {
+    // L_j[p][n] for n = lane + 32 warp + 128 hh (TMEM lane n), p = column
+    float* dst = a.seg_state + ((int64_t)row * a.H + h) * PT * NT;
+    for (int hh = 0; hh < NT / 128; ++hh) {
+      for (int half = 0; half < 2; ++half) {
+        float v[32];
+        ptx::tmem_ld32(tbase + ((uint32_t)(warp * 32) << 16) + 64 * hh + 32 * half, v);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[(int64_t)(32 * half + i) * NT + 128 * hh + r] = v[i];
+      }
+    }
+    if (r == 0) a.seg_tot[(int64_t)row * a.H + h] = total;
+  }
+  // do not leave with copies still landing in shared memory
+  for (int c = nc - SEG_STAGES > 0 ? nc - SEG_STAGES : 0; c < nc && r == 0; ++c)
+    seg_wait(&full[c % SEG_STAGES], (c / SEG_STAGES) & 1, a.status, 5);
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, G_::TCOLS);
+  }
+}
+
+// S_0 = initial state (or 0); S_{j+1} = exp(total dA_j) S_j + L_j, one element per thread.
+__global__ void __launch_bounds__(256) tc_segcombine_kernel(int b, int H, int k, int64_t pn, const float* __restrict__ init,
+                                                          const float* __restrict__ seg_state,
+                                                          const float* __restrict__ seg_tot,
+                                                          float* __restrict__ seg_in) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int bh = blockIdx.y, b0 = bh / H, h = bh % H;
+  if (e >= pn) return;
+  float sv = init ? init[((int64_t)b0 * H + h) * pn + e] : 0.f;
+  for (int j = 0; j < k; ++j) {
+    const int64_t row = (int64_t)b0 * k + j;
+    seg_in[(row * H + h) * pn + e] = sv;
+    if (j + 1 < k) sv = __expf(seg_tot[row * H + h]) * sv + seg_state[(row * H + h) * pn + e];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1321,17 +1566,40 @@ size_t sched_bytes(const ssd_fwd_params_t* p) {
   return p->varlen_states ? (size_t)(8 + 8 * (sched_cap(p) + 1) + 255) / 256 * 256 : 0;
 }
 
+// Segments per batch row of the sequence split (1: none).  Used when few (batch, head)
+// walks would leave most SMs idle: no packed sequences (the segment states then compose by
+// plain decays), chunk-aligned segments of at least two and at most 64 chunks.
+int seg_split(const ssd_fwd_params_t* p) {
+  if (p->seq_idx || p->varlen_states || p->seqlen % QI) return 1;
+  const int64_t bh = p->batch * p->nheads, nci = p->seqlen / QI;
+  if (bh >= 96) return 1;
+  int k = (int)std::min<int64_t>(148 / bh, nci / 2);
+  while (k > 1 && (nci % k || nci / k > 64)) --k;
+  return std::max(k, 1);
+}
+
 // dt pre-pass output: 1 KB per (batch, head, chunk slot).
 int64_t prep_cap(const ssd_fwd_params_t* p) {
-  return p->varlen_states ? sched_cap(p) : (p->seqlen + QI - 1) / QI;
+  return p->varlen_states ? sched_cap(p) : (p->seqlen + QI - 1) / QI / seg_split(p);
 }
-size_t prep_bytes(const ssd_fwd_params_t* p) { return (size_t)p->batch * p->nheads * prep_cap(p) * 2 * QI * 4; }
+size_t prep_bytes(const ssd_fwd_params_t* p) {
+  return (size_t)p->batch * seg_split(p) * p->nheads * prep_cap(p) * 2 * QI * 4;
+}
+// sequence split: L_j and S_j (b*k, H, P, N) f32 each, then the totals (b*k, H)
+size_t seg_bytes(const ssd_fwd_params_t* p) {
+  const int k = seg_split(p);
+  if (k == 1) return 0;
+  const size_t rows = (size_t)p->batch * k * p->nheads;
+  return 2 * rows * PT * p->dstate * 4 + (rows * 4 + 255) / 256 * 256;
+}
 
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
-  return tc_supported(p) ? sched_bytes(p) + prep_bytes(p) + (trace_enabled() ? TRACE_ROLES * 64 * 16 * 8 + 3 * 8 * 2048 : 0) : 0;
+  return tc_supported(p) ? sched_bytes(p) + prep_bytes(p) + seg_bytes(p) +
+                               (trace_enabled() ? TRACE_ROLES * 64 * 16 * 8 + 3 * 8 * 2048 : 0)
+                         : 0;
 }
 
-int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : 2; }
+int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : seg_split(p) > 1 ? 4 : 2; }
 
 // Dynamic shared memory opt-in, per device and kernel variant (the attribute belongs to the
 // current device's context, so a process that drives several GPUs sets it on each).
@@ -1358,7 +1626,9 @@ bool ensure_smem_attr(void (*kern)(TcArgs), int kid) {
 int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace, cudaStream_t st) {
   TcArgs a;
   memset(&a, 0, sizeof(a));
-  const int64_t b = p->batch, L = p->seqlen, H = p->nheads, G = p->ngroups;
+  // with a sequence split the walk runs on the (b*k, L/k) view of the same memory
+  const int k = seg_split(p);
+  const int64_t b = p->batch * k, L = p->seqlen / k, H = p->nheads, G = p->ngroups;
   if (!make_map(&a.tm_x, p->x, (uint64_t)H * PT, L, b) || !make_map(&a.tm_b, p->B, (uint64_t)G * p->dstate, L, b) ||
       !make_map(&a.tm_c, p->C, (uint64_t)G * p->dstate, L, b) ||
       !make_map(&a.tm_out, p->out, (uint64_t)H * PT, L, b, true)) {
@@ -1377,7 +1647,9 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
   float* prep_out = (float*)((char*)workspace + sched_bytes(p));
   a.dtprep = prep_out;
   a.prep_cap = (int)prep_cap(p);
-  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + sched_bytes(p) + prep_bytes(p)) : nullptr;
+  a.seg_k = k;
+  a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + sched_bytes(p) + prep_bytes(p) + seg_bytes(p))
+                            : nullptr;
   typedef void (*KernelFn)(TcArgs);
   static const KernelFn kernels[8] = {
       ssd_fused_tc_kernel<128, false, false>, ssd_fused_tc_kernel<128, false, true>,
@@ -1408,6 +1680,33 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
     const dim3 grid((unsigned)a.prep_cap, (unsigned)b, (unsigned)((H + 3) / 4));
     if (a.dt_bf16) tc_dt_prep_kernel<true><<<grid, 128, 0, st>>>(a, prep_out);
     else tc_dt_prep_kernel<false><<<grid, 128, 0, st>>>(a, prep_out);
+  }
+  if (k > 1) {
+    SegArgs sa;
+    memset(&sa, 0, sizeof(sa));
+    sa.tm_x = a.tm_x;
+    sa.tm_b = a.tm_b;
+    sa.H = (int)H; sa.G = (int)G; sa.k = k; sa.nc = (int)(L / QI); sa.rows = (int)b; sa.lo = p->dt_min;
+    sa.A = p->A; sa.dtprep = prep_out; sa.status = status;
+    const size_t rows = (size_t)b * H, pn = (size_t)PT * p->dstate;
+    float* seg_state = (float*)((char*)workspace + sched_bytes(p) + prep_bytes(p));
+    float* seg_in = seg_state + rows * pn;
+    sa.seg_state = seg_state;
+    sa.seg_tot = seg_in + rows * pn;
+    const unsigned nblk = (unsigned)(p->batch * (k - 1) * H);
+    if (p->dstate == 256) {
+      const uint32_t bytes = SegGeo<256>::BYTES + 1024;
+      cudaFuncSetAttribute(tc_segstate_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      tc_segstate_kernel<256><<<nblk, 128, bytes, st>>>(sa);
+    } else {
+      const uint32_t bytes = SegGeo<128>::BYTES + 1024;
+      cudaFuncSetAttribute(tc_segstate_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      tc_segstate_kernel<128><<<nblk, 128, bytes, st>>>(sa);
+    }
+    const dim3 cgrid((unsigned)((pn + 255) / 256), (unsigned)(p->batch * H));
+    tc_segcombine_kernel<<<cgrid, 256, 0, st>>>((int)p->batch, (int)H, k, (int64_t)pn, p->initial_states, seg_state,
+                                                 sa.seg_tot, seg_in);
+    a.init = seg_in;
   }
   kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
   const cudaError_t e = cudaGetLastError();
