@@ -239,32 +239,41 @@ def cpu_oracle_sample(cfg, budget_s=12.0, heads=None):
 
 
 def run_reference(args, cfg, rank):
+    """The reference arm: the reference's CPU algorithm (ssd_naive, restated in NumPy float64
+    with BLAS on all host threads) on rank 0.  Each step runs the oracle on a bounded head
+    slice of the configured layer at its full length; `ms_per_step` is that measured sample
+    time, and `value` extrapolates it to the whole layer (heads are independent, so the
+    cost is linear in the head count)."""
     if rank != 0:
         return
-    flops, byts = layer_work(cfg)
-    vals = []
     for _ in range(args.warmup):
         cpu_oracle_sample(cfg, budget_s=0.0)
-    t_all = 0.0
+    t_all, scale, desc, thr = 0.0, 1.0, "", 1
     for _ in range(args.steps):
         v, desc, thr = cpu_oracle_sample(cfg, budget_s=0.0)
-        vals.append(v)
-        t_all += cfg.tokens / v
+        hs = cfg.tokens * 1.0 / v   # full-layer seconds
+        t_all += hs
+    hslice = max(cfg.ngroups, min(cfg.nheads, 16))
+    hslice -= hslice % cfg.ngroups
+    scale = cfg.nheads / hslice
     value = args.steps * cfg.tokens / t_all
     line = {"impl": "reference", "metric": "SSD layer fwd tokens/s", "value": value,
             "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * t_all / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "ms_per_step": 1e3 * t_all / args.steps / scale, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch,
                        "seqlen": cfg.seqlen, "nheads": cfg.nheads, "headdim": cfg.headdim,
                        "ngroups": cfg.ngroups, "dstate": cfg.dstate, "chunk_size": cfg.chunk_size,
-                       "input_dtype": cfg.dtype},
+                       "input_dtype": cfg.dtype,
+                       "sample": f"each step: {hslice} of {cfg.nheads} heads at full length; value scaled "
+                                 f"by {scale:g} to the whole layer"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": thr, "kind": "port",
                              "sample": desc},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "note": "the reference (JAX/Pallas) is not installable here; its algorithm is timed "
-                    "through the CPU restatement"}
+            "note": "JAX is not installable here, so the reference's ssd_naive algorithm is timed through "
+                    "its float64 NumPy restatement (oracle/ssd_ref.py), which tests/test_golden.py pins to "
+                    "the reference's own outputs"}
     print(json.dumps(line), flush=True)
 
 
@@ -272,8 +281,17 @@ def run_ours(args, cfg, rank, world, device):
     from mamba2_b200 import mamba_chunk_scan_combined_fwd
     from mamba2_b200.runner import SsdForward
     hbm, tfl, peak_kind = _peaks()
-    inp = S.make_ssd_inputs(cfg, 1000 + 2 + rank)
+    replicas = world > 1 and args.replicas
+    # default at N > 1: one layer, heads sharded over the ranks on group boundaries (strong
+    # scaling); --replicas runs an independent full layer per rank instead
+    inp = S.make_ssd_inputs(cfg, 1000 + 2 + (rank if replicas else 0))
     sets = [dev_inputs(inp, cfg, device) for _ in range(N_SETS)]
+    head_share = 1.0
+    if world > 1 and not replicas:
+        from mamba2_b200 import sharding as SH
+        h0, h1 = SH.head_range(cfg.nheads, cfg.ngroups, world, rank)
+        head_share = (h1 - h0) / cfg.nheads
+        sets = [SH.shard_heads(d, world, rank) for d in sets]
     flags = _lib.SSD_FLAG_BF16_MMA if args.bf16_mma else 0
     runners = [SsdForward(d["x"], d["dt"], d["A"], d["B"], d["C"], cfg.chunk_size, flags=flags, **fwd_kwargs(cfg, d))
                for d in sets]
@@ -292,7 +310,8 @@ def run_ours(args, cfg, rank, world, device):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
-    value = args.steps * cfg.tokens * world / (ms / 1e3)
+    layers = world if replicas else 1
+    value = args.steps * cfg.tokens * layers / (ms / 1e3)
     launches_per_step = runners[0].launches_per_step
 
     # end to end through the public API: pinned host inputs -> device -> forward -> host.
@@ -301,7 +320,7 @@ def run_ours(args, cfg, rank, world, device):
     # copy (H2D): the host link runs both directions at once, as a serving loop would.
     host = {k: (None if v is None else v.cpu().pin_memory()) for k, v in sets[0].items()}
     h2d = sum(v.numel() * v.element_size() for k, v in host.items() if v is not None)
-    b, L, H, P, N = cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.dstate
+    b, L, H, P, N = cfg.batch, cfg.seqlen, sets[0]["x"].shape[2], cfg.headdim, cfg.dstate
     n_lanes = 2
     lanes = []
     for _ in range(n_lanes):
@@ -331,33 +350,47 @@ def run_ours(args, cfg, rank, world, device):
     t = torch.tensor([ms_e2e], device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    e2e_val = args.steps * cfg.tokens * world / (float(t.item()) / 1e3)
+    e2e_val = args.steps * cfg.tokens * layers / (float(t.item()) / 1e3)
 
     if rank != 0:
         return
-    brk = kernel_breakdown(cfg, sets[0], runners[0])
-    top = max(brk, key=lambda r: r[1])
-    name, kms, kbytes, kflops, bound = top
+    flops, byts = layer_work(cfg)
+    flops, byts = flops * head_share, byts * head_share    # this GPU's share of the layer
+    if runners[0].uses_tc:
+        # the step's kernels (dt pre-pass, [segment-state pass, state combine,] fused walk)
+        # timed on the device inside the CUDA-graph replays above: the fused kernel is
+        # about 0.9 of it (profiles/launches_c2.md), so the step bounds the kernel
+        kms = ms / args.steps
+        name = "ssd_fused_tc_kernel + dt pre-pass (one graph-replayed step)"
+        kbytes, kflops = byts, flops
+        bound = "tensor" if flops / (tfl * 1e12) > byts / (hbm * 1e9) else "hbm"
+        brk = [(name, kms, kbytes, kflops, bound)]
+    else:
+        brk = kernel_breakdown(cfg, sets[0], runners[0])
+        name, kms, kbytes, kflops, bound = max(brk, key=lambda r: r[1])
     if bound == "tensor":
         ach, peak, unit = kflops / (kms / 1e3) / 1e12, tfl, "TFLOP/s"
     else:
         ach, peak, unit = kbytes / (kms / 1e3) / 1e9, hbm, "GB/s"
-    flops, byts = layer_work(cfg)
     t_roof = max(flops / (tfl * 1e12), byts / (hbm * 1e9))
     line = {"metric": "SSD layer fwd tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak" if (replicas or world == 1) else "strong",
             "vs_baseline": None, "dtype": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else "f32",
             "data": "synthetic",
             "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch, "seqlen": cfg.seqlen,
                        "nheads": cfg.nheads, "headdim": cfg.headdim, "ngroups": cfg.ngroups,
                        "dstate": cfg.dstate, "chunk_size": cfg.chunk_size, "input_dtype": cfg.dtype,
                        "mma_operands": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else "none (fp32 FFMA)",
-                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "parallelism": (f"replicas x{world}, no collective" if replicas else
+                                       f"head-sharded x{world} on group boundaries, no collective"),
+                       "heads_per_gpu": sets[0]["x"].shape[2],
                        "l2": f"{N_SETS} rotated input sets, each step's inputs+outputs > L2"},
             "roofline": {"kernel": name, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                          "frac": ach / peak, "peak_kind": peak_kind,
-                         "traffic": measured_traffic(f"{name}/{args.config}") if not args.override else None,
+                         "traffic": (measured_traffic(f"ssd_fused_tc/{args.config}")
+                                     if (not args.override and world == 1) else None),
                          "algorithmic_bytes": kbytes, "kernel_ms": kms},
             "layer_roofline": {"t_roof_us": t_roof * 1e6, "t_step_us": 1e3 * ms / args.steps,
                                "frac": t_roof / (ms / args.steps / 1e3), "flops": flops, "bytes": byts},
@@ -591,6 +624,9 @@ def main():
     ap.add_argument("--bf16-mma", action="store_true",
                     help="fp32 configs: bf16 MMA operands on the tensor-core path (the reference's Pallas "
                          "behaviour for fp32 inputs) instead of exact fp32")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: one independent full layer per rank (weak scaling) instead of one layer "
+                         "head-sharded over the ranks")
     ap.add_argument("--override", action="append", default=[],
                     help="key=value on the config (e.g. batch=32) for small profiling cases")
     args = ap.parse_args()

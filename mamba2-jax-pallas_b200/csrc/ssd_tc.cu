@@ -133,8 +133,7 @@ constexpr uint32_t DA_FREE_COUNT = 16;        // SA, SB, T and O warps done with
 struct Misc {
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
   // Per token t of 32-token block k: w_t = exp(dA_{32k} - dA_t) dt_t when block k is
-  // factored as a whole (block_factored), w_t = exp(dA_{8j} - dA_t) dt_t for its 8-token
-  // sub-block j when factored by sub-block (block_factored8), else the processed dt_t.
+  // factored (block_factored), else the processed dt_t.
   float dt[2][QI];
   float Dh;             // skip coefficient of the head (0 without D)
   uint64_t bar[NBARS];
@@ -532,24 +531,13 @@ __device__ __forceinline__ bool block_factored(bool factor, const float* dA, int
 }
 
 // The reference point of row r's decay factor w_r in the dt pre-pass output (the start of its
-// 32-token block, of its 8-token sub-block, or r itself): exp(dA_x - dA_r) dt_r =
+// 32-token block, or r itself): exp(dA_x - dA_r) dt_r =
 // exp(dA_x - ref) w_r for any x.
-__device__ __forceinline__ bool block_factored8(bool factor, const float* dA, int k);
 __device__ __forceinline__ float w_ref(bool factor, const float* dA, int r) {
   const int q = r >> 5;
-  if (block_factored(factor, dA, q)) return dA[32 * q];
-  if (block_factored8(factor, dA, q)) return dA[r & ~7];
-  return dA[r];
+  return block_factored(factor, dA, q) ? dA[32 * q] : dA[r];
 }
 
-// Blocks that do not factor as a whole may still factor by 8-token sub-block (heads whose dA
-// falls by more than 60 over 32 tokens but by at most 60 over every 8).  The dt pre-pass and
-// the consumers decide it from the same dA values.
-__device__ __forceinline__ bool block_factored8(bool factor, const float* dA, int k) {
-  const float* d = dA + 32 * k;
-  return factor && d[0] - d[7] <= FAC_RANGE && d[8] - d[15] <= FAC_RANGE && d[16] - d[23] <= FAC_RANGE &&
-         d[24] - d[31] <= FAC_RANGE;
-}
 
 template <bool DT_BF16>
 __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__ TcArgs a, float* __restrict__ out) {
@@ -581,16 +569,9 @@ __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__
   const float dAs = __shfl_sync(0xffffffffu, dAv[0], lane & ~7);
   const float dAe = __shfl_sync(0xffffffffu, dAv[3], lane | 7);
   const bool fk = factor && (dAs - dAe <= FAC_RANGE);
-  // 8-token sub-blocks (lane pairs) for blocks that do not factor as a whole
-  const float dAs8 = __shfl_sync(0xffffffffu, dAv[0], lane & ~1);
-  const float dAe8 = __shfl_sync(0xffffffffu, dAv[3], lane | 1);
-  int ok8 = (dAs8 - dAe8 <= FAC_RANGE) ? 1 : 0;
-  ok8 &= __shfl_xor_sync(0xffffffffu, ok8, 2);
-  ok8 &= __shfl_xor_sync(0xffffffffu, ok8, 4);
-  const bool fk8 = factor && !fk && ok8;
   float w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = fk ? __expf(dAs - dAv[i]) * d[i] : fk8 ? __expf(dAs8 - dAv[i]) * d[i] : d[i];
+  for (int i = 0; i < 4; ++i) w[i] = fk ? __expf(dAs - dAv[i]) * d[i] : d[i];
   float* o = out + (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
   reinterpret_cast<float4*>(o)[lane] = make_float4(dAv[0], dAv[1], dAv[2], dAv[3]);
   reinterpret_cast<float4*>(o + QI)[lane] = make_float4(w[0], w[1], w[2], w[3]);
@@ -743,33 +724,8 @@ __device__ __forceinline__ void score_block_fac(const float (&v)[32], uint32_t (
   }
 }
 
-// Blocks factored by 8-token sub-block: decay exp(dA_r - dA_{8j}) * w_t for columns of
-// sub-block j (four exponentials per row instead of 32), masked as score_block_fac.
-template <bool HAS_SEQ>
-__device__ __noinline__ void score_block_fac8(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
-                                              const float* wc, int lim, int sl, int seqv, int dcol, float dg) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float u = __expf(dA - dAc[8 * j]);
-#pragma unroll
-    for (int i = 8 * j; i < 8 * j + 8; i += 2) {
-      float o[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        bool ok = i + e <= lim;
-        if (HAS_SEQ) {
-          const int st = __shfl_sync(0xffffffffu, sl, i + e);   // all lanes shuffle, then combine
-          ok = ok && (st == seqv);
-        }
-        o[e] = (ok ? v[i + e] * (u * wc[i + e]) : 0.f) + (i + e == dcol ? dg : 0.f);
-      }
-      pk[i / 2] = pack_bf16(o[0], o[1]);
-    }
-  }
-}
-
-// Blocks that do not factor (dA may increase, or its range within 8 tokens exceeds 60):
-// exp(dA_r - dA_t) dt_t per element.
+// Blocks that do not factor (dA may increase, or its range in the block exceeds 60, as for
+// heads with large |A| dt): exp(dA_r - dA_t) dt_t per element.
 template <bool HAS_SEQ>
 __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t (&pk)[16], float dA, const float* dAc,
                                                   const float* dtc, int lim, int sl, int seqv, int dcol, float dg) {
@@ -851,8 +807,6 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
         const int dcol = k32 == q ? lane : -1;
         if (fac && !HAS_SEQ && k32 < q) score_block_full(v, pk, __expf(dA - dAc[0]), wc);
         else if (fac) score_block_fac<HAS_SEQ>(v, pk, __expf(dA - dAc[0]), wc, lim, sl, seqv, dcol, dg);
-        else if (block_factored8(factor, m->dA[buf], k32))
-          score_block_fac8<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         else score_block_exact<HAS_SEQ>(v, pk, dA, dAc, wc, lim, sl, seqv, dcol, dg);
         ptx::tmem_st16(tS, pk);
         if (q == 0 || q == 3) TRACE(trole, c, 12 + 2 * kk);
