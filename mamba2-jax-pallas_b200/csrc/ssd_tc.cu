@@ -1283,14 +1283,13 @@ struct SegArgs {
   unsigned* status;
 };
 
-constexpr int SEG_STAGES = 2;
-
 template <int NT>
 struct SegGeo {
+  static constexpr int STAGES = NT == 256 ? 2 : 4;        // B + x tiles of that many chunks in flight
   static constexpr uint32_t SZ_B = QI * NT * 2;         // B tile of one chunk
   static constexpr uint32_t SZ_X = QI * PT * 2;         // x tile
   static constexpr uint32_t SZ_STAGE = SZ_B + SZ_X;
-  static constexpr uint32_t OFF_XS = SEG_STAGES * SZ_STAGE;   // two xs buffers
+  static constexpr uint32_t OFF_XS = STAGES * SZ_STAGE;   // two xs buffers
   static constexpr uint32_t BYTES = OFF_XS + 2 * SZ_X;
   static constexpr uint32_t TCOLS = NT == 256 ? 128 : 64;
 };
@@ -1306,12 +1305,32 @@ __device__ __forceinline__ bool seg_wait(uint64_t* bar, uint32_t parity, unsigne
   return true;
 }
 
+// What row r of chunk c needs from the pre-pass output: dA_last - ref and w_r.
+struct SegRow {
+  float e, w;
+};
+__device__ __forceinline__ SegRow seg_row(const float* dA, bool factor, int r) {
+  const int q = r >> 5;
+  const float last = dA[QI - 1], d0 = dA[32 * q], d31 = dA[32 * q + 31], dr = dA[r];
+  const bool fq = factor && (d0 - d31 <= FAC_RANGE);   // block_factored on the same values
+  return {last - (fq ? d0 : dr), dA[QI + r]};
+}
+
+template <int NT>
+__device__ __forceinline__ void seg_load(const SegArgs& a, uint8_t* st, uint64_t* bar, int g, int h, int c, int row) {
+  using G_ = SegGeo<NT>;
+  ptx::mbar_arrive_expect_tx(bar, G_::SZ_STAGE);
+  for (int hh = 0; hh < NT / 64; ++hh) ptx::tma_load_3d(st + hh * (QI * 128), &a.tm_b, bar, g * NT + 64 * hh, c * QI, row);
+  ptx::tma_load_3d(st + G_::SZ_B, &a.tm_x, bar, h * PT, c * QI, row);
+}
+
 template <int NT>
 __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_constant__ SegArgs a) {
   using G_ = SegGeo<NT>;
+  constexpr int ST = G_::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t full[SEG_STAGES], done[2], fin;
+  __shared__ uint64_t full[ST], done[2], fin;
   __shared__ uint32_t tbase;
   __shared__ float tots[64];
   __shared__ volatile int bad;
@@ -1324,7 +1343,7 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
   const int nc = a.nc;
   const float* prep = a.dtprep + ((int64_t)row * a.H + h) * nc * (2 * QI);
   if (r == 0) {
-    for (int i = 0; i < SEG_STAGES; ++i) ptx::mbar_init(&full[i], 1);
+    for (int i = 0; i < ST; ++i) ptx::mbar_init(&full[i], 1);
     ptx::mbar_init(&done[0], 1);
     ptx::mbar_init(&done[1], 1);
     ptx::mbar_init(&fin, 1);
@@ -1340,34 +1359,33 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  if (r == 0) {
-    for (int c = 0; c < nc && c < SEG_STAGES; ++c) {
-      uint8_t* st = sm + c * G_::SZ_STAGE;
-      ptx::mbar_arrive_expect_tx(&full[c], G_::SZ_STAGE);
-      for (int hh = 0; hh < NT / 64; ++hh) ptx::tma_load_3d(st + hh * (QI * 128), &a.tm_b, &full[c], g * NT + 64 * hh, c * QI, row);
-      ptx::tma_load_3d(st + G_::SZ_B, &a.tm_x, &full[c], h * PT, c * QI, row);
-    }
-  }
+  if (r == 0)
+    for (int c = 0; c < nc && c < ST; ++c) seg_load<NT>(a, sm + c * G_::SZ_STAGE, &full[c], g, h, c, row);
   const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);
   float suffix = 0.f;
   for (int c = 0; c < nc; ++c) suffix += tots[c];   // total dA of the segment
   const float total = suffix;
   constexpr uint32_t ID_L = ptx::idesc_bf16_f32(128, 64, 1, 1);
+  SegRow nxt = seg_row(prep, factor, r);            // chunk 0's factors, then one chunk ahead
   for (int c = 0; c < nc; ++c) {
     suffix -= tots[c];                               // dA of the chunks after c
-    const int s = c % SEG_STAGES;
-    // xs(c): row r of x scaled by exp(dA_end - dA_r) dt_r, into buffer c % 2 once MMA(c-2) is done
-    const float* dA = prep + (int64_t)c * 2 * QI;
-    const float scale = __expf(suffix + dA[QI - 1] - w_ref(factor, dA, r)) * dA[QI + r];
+    const int s = c % ST;
+    const SegRow cur = nxt;
+    if (c + 1 < nc) nxt = seg_row(prep + (int64_t)(c + 1) * 2 * QI, factor, r);
+    // exp(dA_end - dA_r) dt_r = exp(suffix + dA_last - ref) w_r
+    const float scale = __expf(suffix + cur.e) * cur.w;
+    // xs buffer c % 2 is free once MMA(c-2) is done; the tiles of chunk c have landed
     if (c >= 2 && !seg_wait(&done[c & 1], ((c >> 1) - 1) & 1, a.status, 1)) bad = 1;
-    if (!seg_wait(&full[s], (c / SEG_STAGES) & 1, a.status, 2)) bad = 1;
-    __syncthreads();   // every thread sees the same `bad` (waits above are bounded)
+    if (!seg_wait(&full[s], (c / ST) & 1, a.status, 2)) bad = 1;
+    __syncthreads();   // every thread sees the same `bad` (the waits above are bounded)
     if (bad) break;
     const uint8_t* xt = sm + s * G_::SZ_STAGE + G_::SZ_B;
     uint8_t* xs = sm + G_::OFF_XS + (c & 1) * G_::SZ_X;
+    uint4 w[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      *reinterpret_cast<uint4*>(xs + ptx::sw128_off(r, k)) = scale_row16(*reinterpret_cast<const uint4*>(xt + ptx::sw128_off(r, k)), scale);
+    for (int k = 0; k < 8; ++k) w[k] = *reinterpret_cast<const uint4*>(xt + ptx::sw128_off(r, k));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) *reinterpret_cast<uint4*>(xs + ptx::sw128_off(r, k)) = scale_row16(w[k], scale);
     ptx::fence_proxy_async_smem();
     __syncthreads();
     if (r == 0) {
@@ -1382,18 +1400,11 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
                        (c > 0 || i > 0) ? 1u : 0u);
       }
       ptx::mma_commit(&done[c & 1]);
-      // refill this stage with chunk c + SEG_STAGES once MMA(c) has read it
-      if (c + SEG_STAGES < nc) {
-        if (!seg_wait(&done[c & 1], (c >> 1) & 1, a.status, 3)) {
-          bad = 1;
-        } else {
-          uint8_t* st = sm + s * G_::SZ_STAGE;
-          const int cn = c + SEG_STAGES;
-          ptx::mbar_arrive_expect_tx(&full[s], G_::SZ_STAGE);
-          for (int hh = 0; hh < NT / 64; ++hh)
-            ptx::tma_load_3d(st + hh * (QI * 128), &a.tm_b, &full[s], g * NT + 64 * hh, cn * QI, row);
-          ptx::tma_load_3d(st + G_::SZ_B, &a.tm_x, &full[s], h * PT, cn * QI, row);
-        }
+      // refill the stage of chunk c-1 (its MMA was issued an iteration ago) with chunk c-1+ST
+      const int cr = c - 1 + ST;
+      if (c >= 1 && cr < nc) {
+        if (!seg_wait(&done[(c - 1) & 1], ((c - 1) >> 1) & 1, a.status, 3)) bad = 1;
+        else seg_load<NT>(a, sm + ((c - 1) % ST) * G_::SZ_STAGE, &full[(c - 1) % ST], g, h, cr, row);
       }
     }
   }
@@ -1414,9 +1425,13 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
     }
     if (r == 0) a.seg_tot[(int64_t)row * a.H + h] = total;
   }
-  // do not leave with copies still landing in shared memory
-  for (int c = nc - SEG_STAGES > 0 ? nc - SEG_STAGES : 0; c < nc && r == 0; ++c)
-    seg_wait(&full[c % SEG_STAGES], (c / SEG_STAGES) & 1, a.status, 5);
+  // do not leave with copies still landing in shared memory: the last load of every stage
+  if (r == 0) {
+    for (int st = 0; st < ST && st < nc; ++st) {
+      const int last = st + ((nc - 1 - st) / ST) * ST;   // last chunk loaded into stage st
+      seg_wait(&full[st], (last / ST) & 1, a.status, 5);
+    }
+  }
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
