@@ -167,6 +167,8 @@ struct TcArgs {
   unsigned* status;
   long long test_wait_cycles;  // > 0: test mode, see the start of ssd_fused_tc_kernel
   int seg_k;                   // rows per batch row when the sequence is split (1: no split)
+  const float* seg_state;      // split: L_j of every segment but the last, (b*seg_k, H, P, N)
+  const float* seg_tot;        // split: total dA of each segment, (b*seg_k, H)
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
@@ -903,7 +905,8 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const int64_t bh = (int64_t)bi * a.H + h;
   // with a split sequence, row bi is segment bi % seg_k of batch row bi / seg_k: only the
   // last segment's state is a final state
-  const int64_t fbh = (int64_t)(bi / a.seg_k) * a.H + h;
+  const int64_t ib = bi / a.seg_k, fbh = ib * a.H + h;
+  const int jseg = bi % a.seg_k;
   float* const fin = (bi % a.seg_k == a.seg_k - 1) ? a.final_states : nullptr;
   const int nci = m->nci;
   if (nci <= 0) return;
@@ -918,7 +921,23 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     const int n = hh * 128 + r;
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = a.init ? a.init[(bh * PT + 32 * half + i) * NT + n] : 0.f;
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    // S_j = sum_{l<j} exp(total dA of segments l+1..j-1) L_l + exp(total dA of 0..j-1) S_init
+    // (segment j = bi % seg_k of batch row bi / seg_k; without a split j = 0, S_0 = S_init)
+    float sdA = 0.f;
+    for (int l = jseg - 1; l >= 0; --l) {
+      const int64_t lr = (ib * a.seg_k + l) * a.H + h;
+      const float coef = __expf(sdA);
+      const float* Ll = a.seg_state + lr * PT * NT + n;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaf(coef, __ldcg(Ll + (32 * half + i) * NT), v[i]);
+      sdA += __ldcg(a.seg_tot + lr);
+    }
+    if (a.init) {
+      const float coef = __expf(sdA);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaf(coef, a.init[((ib * a.H + h) * PT + 32 * half + i) * NT + n], v[i]);
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
@@ -1266,8 +1285,8 @@ __global__ void __launch_bounds__(SCHED_THREADS) tc_schedule_kernel(const int32_
 //                       from a zero start, L_j = sum_t exp(dA_end - dA_t) dt_t B_t^T x_t
 //                       (one tcgen05 accumulation over the segment's tokens; each token's
 //                       x row is scaled in shared memory), and its total dA
-//   tc_segcombine_kernel S_0 = initial state, S_{j+1} = exp(total dA_j) S_j + L_j
-// and the fused kernel then runs every segment from its S_j.  Only the state recurrence
+// and the fused kernel's state warps start segment j from
+//   S_j = sum_{l<j} exp(total dA of segments l+1..j-1) L_l + exp(total dA of 0..j-1) S_init.  Only the state recurrence
 // crosses segments (state_passing_fwd.py:108-151 restated over segments), so outputs and
 // the final state equal the unsplit walk up to rounding.
 // ---------------------------------------------------------------------------
@@ -1440,21 +1459,6 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
   }
 }
 
-// S_0 = initial state (or 0); S_{j+1} = exp(total dA_j) S_j + L_j, one element per thread.
-__global__ void __launch_bounds__(256) tc_segcombine_kernel(int b, int H, int k, int64_t pn, const float* __restrict__ init,
-                                                          const float* __restrict__ seg_state,
-                                                          const float* __restrict__ seg_tot,
-                                                          float* __restrict__ seg_in) {
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int bh = blockIdx.y, b0 = bh / H, h = bh % H;
-  if (e >= pn) return;
-  float sv = init ? init[((int64_t)b0 * H + h) * pn + e] : 0.f;
-  for (int j = 0; j < k; ++j) {
-    const int64_t row = (int64_t)b0 * k + j;
-    seg_in[(row * H + h) * pn + e] = sv;
-    if (j + 1 < k) sv = __expf(seg_tot[row * H + h]) * sv + seg_state[(row * H + h) * pn + e];
-  }
-}
 
 // ---------------------------------------------------------------------------
 // host side
@@ -1554,12 +1558,12 @@ int64_t prep_cap(const ssd_fwd_params_t* p) {
 size_t prep_bytes(const ssd_fwd_params_t* p) {
   return (size_t)p->batch * seg_split(p) * p->nheads * prep_cap(p) * 2 * QI * 4;
 }
-// sequence split: L_j and S_j (b*k, H, P, N) f32 each, then the totals (b*k, H)
+// sequence split: L_j (b*k, H, P, N) f32, then the segment totals (b*k, H)
 size_t seg_bytes(const ssd_fwd_params_t* p) {
   const int k = seg_split(p);
   if (k == 1) return 0;
   const size_t rows = (size_t)p->batch * k * p->nheads;
-  return 2 * rows * PT * p->dstate * 4 + (rows * 4 + 255) / 256 * 256;
+  return rows * PT * p->dstate * 4 + (rows * 4 + 255) / 256 * 256;
 }
 
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
@@ -1568,7 +1572,7 @@ size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
                          : 0;
 }
 
-int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : seg_split(p) > 1 ? 4 : 2; }
+int tc_num_launches(const ssd_fwd_params_t* p) { return p->varlen_states ? 3 : seg_split(p) > 1 ? 3 : 2; }
 
 // Dynamic shared memory opt-in, per device and kernel variant (the attribute belongs to the
 // current device's context, so a process that drives several GPUs sets it on each).
@@ -1659,9 +1663,8 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
     sa.A = p->A; sa.dtprep = prep_out; sa.status = status;
     const size_t rows = (size_t)b * H, pn = (size_t)PT * p->dstate;
     float* seg_state = (float*)((char*)workspace + sched_bytes(p) + prep_bytes(p));
-    float* seg_in = seg_state + rows * pn;
     sa.seg_state = seg_state;
-    sa.seg_tot = seg_in + rows * pn;
+    sa.seg_tot = seg_state + rows * pn;
     const unsigned nblk = (unsigned)(p->batch * (k - 1) * H);
     if (p->dstate == 256) {
       const uint32_t bytes = SegGeo<256>::BYTES + 1024;
@@ -1672,10 +1675,8 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
       cudaFuncSetAttribute(tc_segstate_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
       tc_segstate_kernel<128><<<nblk, 128, bytes, st>>>(sa);
     }
-    const dim3 cgrid((unsigned)((pn + 255) / 256), (unsigned)(p->batch * H));
-    tc_segcombine_kernel<<<cgrid, 256, 0, st>>>((int)p->batch, (int)H, k, (int64_t)pn, p->initial_states, seg_state,
-                                                 sa.seg_tot, seg_in);
-    a.init = seg_in;
+    a.seg_state = seg_state;
+    a.seg_tot = sa.seg_tot;
   }
   kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
   const cudaError_t e = cudaGetLastError();

@@ -23,11 +23,11 @@ def _need_gpu():
 
 CASES = [
     # one rank of c2 head-sharded over 8 GPUs: 16 heads, 2 groups -> 8 segments of 512 tokens
-    ("c2-rank-of-8", S.scaled(S.CONFIGS["c2"], nheads=16, ngroups=2), 4),
+    ("c2-rank-of-8", S.scaled(S.CONFIGS["c2"], nheads=16, ngroups=2), 3),
     # one rank of c2 over 4 GPUs, with the z gate
-    ("c2-rank-of-4-z", S.scaled(S.CONFIGS["c2"], nheads=32, ngroups=2, has_z=True), 4),
+    ("c2-rank-of-4-z", S.scaled(S.CONFIGS["c2"], nheads=32, ngroups=2, has_z=True), 3),
     # N = 256, two batch rows, no initial state
-    ("n256-b2", S.SsdConfig("n256", 2, 2048, 8, 64, 1, 256, 128, "bf16", return_final=True), 4),
+    ("n256-b2", S.SsdConfig("n256", 2, 2048, 8, 64, 1, 256, 128, "bf16", return_final=True), 3),
 ]
 
 
