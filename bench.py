@@ -406,6 +406,64 @@ def run_ours(args, cfg, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_sp(args, cfg, rank, world, device):
+    """--sp: the sequence-parallel variant of a packed config (c3): rank r holds a
+    chunk-aligned token segment of the packed row, runs it from a zero state, receives the
+    state entering it by the recursive-doubling exchange over NCCL and adds it with the
+    tensor-core fix-up (mamba2_b200.sharding.ssd_forward_sequence_parallel).  value = the
+    row's tokens / the slowest rank's time per step.  Inputs are drawn on the device (seeded
+    per rank) with the config's distributions; the packed lengths come from the config's
+    seeded generator."""
+    from mamba2_b200 import sharding as SH
+    g = torch.Generator(device=device).manual_seed(5000 + rank)
+    rng = np.random.default_rng(77)
+    L, H, P, G, N, Q = cfg.seqlen, cfg.nheads, cfg.headdim, cfg.ngroups, cfg.dstate, cfg.chunk_size
+    t0, t1 = SH.seq_segment(L, Q, world, rank)
+    n = t1 - t0
+    seq_full = np.zeros(L, np.int32)
+    if cfg.varlen_seqs:
+        lens = S.varlen_lengths(rng, cfg.varlen_seqs, L, *cfg.varlen_range)
+        seq_full = np.repeat(np.arange(len(lens), dtype=np.int32), lens)
+    rn = lambda *shape: torch.randn(shape, generator=g, device=device).to(torch.bfloat16)
+    x, dt, B, C = rn(1, n, H, P), rn(1, n, H), rn(1, n, G, N), rn(1, n, G, N)
+    dt0 = np.exp(rng.uniform(math.log(1e-3), math.log(0.1), size=H))
+    dt_bias = torch.from_numpy((dt0 + np.log(-np.expm1(-dt0))).astype(np.float32)).to(device)
+    A = torch.from_numpy((-np.exp(np.log(rng.uniform(1.0, 16.0, size=H)))).astype(np.float32)).to(device)
+    D = torch.ones(H, device=device)
+    seq = torch.from_numpy(seq_full[t0:t1][None].copy()).to(device)
+    prev = torch.tensor([int(seq_full[t0 - 1]) if t0 > 0 else 0], dtype=torch.int32, device=device)
+
+    def step(_i):
+        return SH.ssd_forward_sequence_parallel(x, dt, A, B, C, Q, D=D, dt_bias=dt_bias, seq_idx=seq,
+                                                prev_seq=prev, dt_softplus=True)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    stream = torch.cuda.current_stream()
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(step, args.steps, stream)
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = clk.stop() if clk else None
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank != 0:
+        return
+    line = {"metric": "SSD layer fwd tokens/s (sequence parallel)", "value": args.steps * L / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "key": args.config, "seqlen": L, "nheads": H, "headdim": P,
+                       "ngroups": G, "dstate": N, "chunk_size": Q, "packed_sequences": cfg.varlen_seqs,
+                       "parallelism": f"sequence-parallel x{world}: zero-state segment forward, recursive-"
+                                      f"doubling state exchange over NCCL, tensor-core fix-up"},
+            "gpu_launches": None, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def run_ssu(args, rank, world, device):
     """c4: selective_state_update decode steps, state updated in place (1000 steps timed as
     one region; tokens = batch x steps)."""
@@ -624,6 +682,8 @@ def main():
     ap.add_argument("--bf16-mma", action="store_true",
                     help="fp32 configs: bf16 MMA operands on the tensor-core path (the reference's Pallas "
                          "behaviour for fp32 inputs) instead of exact fp32")
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence-parallel variant of the config (c3): token segments over the ranks")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: one independent full layer per rank (weak scaling) instead of one layer "
                          "head-sharded over the ranks")
@@ -646,7 +706,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
+    if world > 1 or args.sp:
+        if world == 1:   # the sequence-parallel path runs its exchange even on one rank
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
         torch.distributed.init_process_group("nccl", device_id=device)
     try:
         if args.config == "c4":
@@ -655,10 +720,12 @@ def main():
             run_conv(args, rank, world, device)
         elif args.config == "norm":
             run_norm(args, rank, world, device)
+        elif args.sp:
+            run_sp(args, cfg, rank, world, device)
         else:
             run_ours(args, cfg, rank, world, device)
     finally:
-        if world > 1:
+        if world > 1 or args.sp:
             torch.distributed.destroy_process_group()
 
 

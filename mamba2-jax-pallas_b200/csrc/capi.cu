@@ -447,6 +447,7 @@ int ssd_sp_state_fixup(const ssd_sp_fixup_params_t* p, ssd_stream_t stream) {
   if (!dtype_ok(p->dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
   if (!p->C || !p->dA_cumsum || !p->state_in || !p->out)
     return fail(SSD_ERR_INVALID_ARG, "C, dA_cumsum, state_in and out are required");
+  if (ssd::tc_sp_fixup_supported(p)) return ssd::tc_sp_fixup(p, (cudaStream_t)stream);
   return cuda_status(ssd::launch_sp_fixup(p, (cudaStream_t)stream), "sp_state_fixup");
 }
 

@@ -24,19 +24,17 @@
 // float range); other blocks are formed element by element.
 //
 // The only serial dependence between chunks is the state: E3(c) -> MMA3(c+1) -> E3(c+1).
-// Everything else is pipelined around it by warp role (20 warps in five warpgroups; every
-// SM sub-partition holds 5 warps; the single-lane roles give registers to the workers):
+// Everything else is pipelined around it by warp role (16 warps, so every SM sub-partition
+// holds 4 warps and each thread may use 128 registers):
 //   warp 0      MMA issuer B (lane 0): MMA3, MMA_L (the state chain)
 //   warp 1      MMA issuer A (lane 0): MMA1, MMA2; owns the TMEM allocation (512 columns)
 //   warp 2      TMA producer (lane 0)
 //   warp 3      dA producer (lane 0): the chunk's cumulative dA and decay factors, computed
 //               by the dt pre-pass, bulk-copied into shared memory
-//   warps 4-7   SA: score column blocks 0 and 2 of each row quadrant
-//   warps 8-11  SB: score column blocks 1 and 3
-//   warps 12-15 T: the state recurrence E3 (bf16 copy for MMA3, decay for MMA_L) and xs of
-//               the next chunk (E1, double-buffered)
-//   warps 16-19 O: the output epilogue E4 (staged in shared memory one 32-column box at a
-//               time, written by TMA bulk stores), in parallel with T
+//   warps 4-7   SA: xs columns 0-31, score column blocks 0 and 2 of each row quadrant
+//   warps 8-11  SB: xs columns 32-63, score column blocks 1 and 3
+//   warps 12-15 T: the state recurrence E3 and the output epilogue E4 of the previous chunk
+//               (staged in shared memory, written by TMA bulk stores)
 // MMA_L accumulates the chunk's state contribution L_c in its own TMEM columns, so xs and
 // MMA_L do not wait for the state chain.  The bf16 scores go back into TMEM (over the CB
 // columns already read) and MMA2 takes them from there as its A operand.  Warp w reads TMEM lanes 32*(w%4)..+31, i.e. chunk
@@ -62,16 +60,7 @@ namespace {
 
 constexpr int QI = 128;       // internal chunk (tokens)
 constexpr int PT = 64;        // head dim handled by the kernel
-constexpr int NTHREADS = 640;
-// Registers: the block launches at 96 per thread (640 x 96 = 61440 of the SM's 65536); the
-// single-lane role warpgroup (warps 0-3) gives up registers and the four worker warpgroups
-// take 104 each.  The roles keep 40 at N = 128 and 64 at N = 256 (longer MMA loops):
-// 128 x 64 + 512 x 104 = 61440, so every setmaxnreg.inc can complete.  The host checks
-// that the kernel really launches with LAUNCH_REGS before the first launch.
-constexpr int LAUNCH_REGS = 96, WORKER_REGS = 104;
-template <int NT>
-__host__ __device__ constexpr int role_regs() { return NT == 256 ? 64 : 40; }
-static_assert(128 * 64 + 512 * WORKER_REGS <= NTHREADS * LAUNCH_REGS, "register split");
+constexpr int NTHREADS = 512;
 // Single-lane roles of warps 0-3.  Warp w issues on SM sub-partition w % 4, which it shares
 // with the score and state warps of row quadrant w % 4; quadrant 3 has the most score work
 // (four 32-column blocks against one in quadrant 0), so the lightest role sits on 3 and
@@ -107,10 +96,9 @@ struct Geo {
   static constexpr uint32_t SZ_X = QI * PT * 2;     // 16 KB
   static constexpr uint32_t OFF_CB = 0;
   static constexpr uint32_t OFF_X = 2 * SZ_CBST;
-  static constexpr uint32_t SZ_STAGE = QI * 32 * 4;  // one 32-column f32 output box: 16 KB
   static constexpr uint32_t OFF_S = OFF_X + XST * SZ_X;
-  static constexpr uint32_t OFF_XS = OFF_S + SZ_STAGE;  // two xs buffers
-  static constexpr uint32_t OFF_ST = OFF_XS + 2 * SZ_X;
+  static constexpr uint32_t OFF_XS = OFF_S + QI * QI * 2;
+  static constexpr uint32_t OFF_ST = OFF_XS + SZ_X;
   static constexpr uint32_t OFF_MISC = OFF_ST + NT * PT * 2;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + MISC_BYTES;
   static constexpr uint32_t COL_ST = COL_YI0 + 64 * YIB;
@@ -122,13 +110,13 @@ struct Geo {
 // has consumed the current phase is per buffer (B_CB, CB_FREE, S_FULL_*, B_YI, YI_FREE), so
 // no waiter can see a phase parity two phases late.
 enum Bar { CB_FULL0, CB_FULL1, CB_EMPTY0, CB_EMPTY1, X_FULL0, X_FULL1, X_EMPTY0, X_EMPTY1, B_CB0, B_CB1,
-           CB_FREE0, CB_FREE1, XS_FULL0, XS_FULL1, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1,
-           ST_READY, SCALED, B_L, B_Y0, B_Y1, B_YI0, B_YI1, Y_FREE0, Y_FREE1, YI_FREE0, YI_FREE1, DA_READY0, DA_READY1, DA_FREE0,
+           CB_FREE0, CB_FREE1, XS_FULL, S_FULL_A0, S_FULL_A1, S_FULL_B0, S_FULL_B1,
+           ST_READY, SCALED, B_L, XS_FREE, B_Y0, B_Y1, B_YI0, B_YI1, Y_FREE0, Y_FREE1, YI_FREE0, YI_FREE1, DA_READY0, DA_READY1, DA_FREE0,
            DA_FREE1, OUT_READ, STAGED, DRAIN, NBARS };
 
 // arrivals per phase
-constexpr uint32_t X_EMPTY_COUNT = 1 + 4;   // MMA2 commit and the T warps (xs built)
-constexpr uint32_t DA_FREE_COUNT = 16;        // SA, SB, T and O warps done with a chunk's dA/dt arrays
+constexpr uint32_t X_EMPTY_COUNT = 1 + 4 + 4;   // MMA2 commit, SA and SB warps (their halves of xs)
+constexpr uint32_t DA_FREE_COUNT = 12;        // SA, SB and T warps done with a chunk's dA/dt arrays
 
 struct Misc {
   float dA[2][QI];      // per-chunk cumulative dt*A, double-buffered by chunk parity
@@ -172,16 +160,13 @@ struct TcArgs {
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
 };
 
-// Debug trace: SM cycle counter at phase boundaries of CTA 0, slot [role][chunk][phase]
-// (roles 0-3 score warps SA q0, SA q3, SB q0, SB q3; 4 MMA issuers; 5 T; 6 producer; 7 score
-// warps q1/q2; 8, 9 O q0, q3), then per CTA {start globaltimer, end globaltimer, SM id}.
-// Compiled in only with -DSSD_TC_DEBUG_TRACE (and then enabled at run time by SSD_TC_TRACE=1).
-constexpr int TRACE_ROLES = 10;
+// Debug trace: globaltimer at phase boundaries of CTA 0, slot [role][chunk][phase].  Compiled
+// in only with -DSSD_TC_DEBUG_TRACE (and then enabled at run time by SSD_TC_TRACE=1).
 #ifdef SSD_TC_DEBUG_TRACE
 #define TRACE(role, c, ph)                                                                       \
   do {                                                                                           \
     if (a.trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (c) < 64)                      \
-      a.trace[((role) * 64 + (c)) * 16 + (ph)] = clock64();                                      \
+      a.trace[((role) * 64 + (c)) * 16 + (ph)] = ptx::globaltimer();                             \
   } while (0)
 #else
 #define TRACE(role, c, ph) \
@@ -198,10 +183,6 @@ constexpr long long TIMEOUT_CYCLES = 4000000000LL;
 // when another role of this CTA already gave up.  One probe is inlined; the spin loop is
 // a single out-of-line copy, so the many wait sites add little to the hot code (which
 // otherwise outgrows the instruction cache).
-// RG selects one out-of-line copy per register budget (0: the single-lane roles, 1: the
-// worker warpgroups); ptxas cannot allocate one non-inlined function for two setmaxnreg
-// budgets.
-template <int RG>
 __device__ __noinline__ bool wait_bar_slow(Misc* m, int id, uint32_t parity, unsigned* status) {
   const long long t0 = clock64();
   while (true) {
@@ -218,15 +199,9 @@ __device__ __noinline__ bool wait_bar_slow(Misc* m, int id, uint32_t parity, uns
   }
 }
 
-// roles (warps 0-3)
 __device__ __forceinline__ bool wait_bar(Misc* m, int id, uint32_t parity, unsigned* status) {
   if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
-  return wait_bar_slow<0>(m, id, parity, status);
-}
-// worker warpgroups (warps 4-19)
-__device__ __forceinline__ bool wait_barw(Misc* m, int id, uint32_t parity, unsigned* status) {
-  if (ptx::mbar_try_wait(&m->bar[id], parity)) return true;
-  return wait_bar_slow<1>(m, id, parity, status);
+  return wait_bar_slow(m, id, parity, status);
 }
 
 // silu(v) = v sigmoid(v) = 0.5 v (1 + tanh(v / 2)): one tanh.approx (relative error about
@@ -446,7 +421,7 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
     }
     // MMA_L first: it does not wait for the previous output
     // MMA_L: S_{c+1} = (scaled S_c) + B^T . xs, one 128-row half of the state dim per stage
-    if (!wait_bar(m, XS_FULL0 + (c & 1), (c >> 1) & 1, a.status)) goto drain;
+    if (!wait_bar(m, XS_FULL, c & 1, a.status)) goto drain;
     if (!wait_bar(m, SCALED, c & 1, a.status)) goto drain;
     ptx::tc_fence_after();
     for (int hh = 0; hh < G_::NH; ++hh) {
@@ -454,8 +429,9 @@ __device__ void mma_issuer_b(const TcArgs& a, uint8_t* sm, Misc* m) {
 #pragma unroll
       for (int i = 0; i < QI / 16; ++i)
         ptx::mma_f16(tmem + G_::COL_ST + 64 * hh, ptx::sdesc_sw128(sB + i * 2048, G_::SZ_H / 2, 1024),
-                     ptx::sdesc_sw128(base + G_::OFF_XS + (c & 1) * G_::SZ_X + i * 2048, 8192, 1024), ID_L, 1u);
+                     ptx::sdesc_sw128(base + G_::OFF_XS + i * 2048, 8192, 1024), ID_L, 1u);
     }
+    ptx::mma_commit(&m->bar[XS_FREE]);   // MMA_L(c) done with xs
     TRACE(4, c, 3);
     // MMA3: Yi = C . S_c^T (B operand = bf16 state [n][p], MN-major)
     if (!wait_bar(m, ST_READY, c & 1, a.status)) goto drain;
@@ -532,15 +508,6 @@ __device__ __forceinline__ bool block_factored(bool factor, const float* dA, int
   return factor && (dA[32 * k] - dA[32 * k + 31] <= FAC_RANGE);
 }
 
-// The reference point of row r's decay factor w_r in the dt pre-pass output (the start of its
-// 32-token block, or r itself): exp(dA_x - dA_r) dt_r =
-// exp(dA_x - ref) w_r for any x.
-__device__ __forceinline__ float w_ref(bool factor, const float* dA, int r) {
-  const int q = r >> 5;
-  return block_factored(factor, dA, q) ? dA[32 * q] : dA[r];
-}
-
-
 template <bool DT_BF16>
 __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__ TcArgs a, float* __restrict__ out) {
   const int c = blockIdx.x, bi = blockIdx.y;
@@ -579,9 +546,9 @@ __global__ void __launch_bounds__(128) tc_dt_prep_kernel(const __grid_constant__
   reinterpret_cast<float4*>(o + QI)[lane] = make_float4(w[0], w[1], w[2], w[3]);
 }
 
-// Output epilogue of chunk c (run by O): out = Y + sdec Yi, z gate (Y holds D x).  Row r is
-// staged as f32 in a 16 KB buffer, one 128B-swizzled [128][32] box at a time, and each box
-// is written by one TMA bulk store, so global writes are full lines.  The inner
+// Output epilogue of chunk c (run by T): out = Y + sdec Yi, z gate (Y holds D x).  Row r is
+// staged as f32 in the (free) score buffer as two 128B-swizzled [128][32] boxes and
+// written by one TMA bulk store per box, so global writes are full lines.  The inner
 // loops carry no data-dependent branches (each costs tens of cycles when unrolled).
 template <int NT, bool HAS_Z>
 __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tmem, int bi, int h, int c, int r,
@@ -602,22 +569,21 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
 #pragma unroll
     for (int k = 0; k < 8; ++k) zq[k] = __ldg(zp + k);
   }
-  if (!wait_barw(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
-  if (!wait_barw(m, B_YI0 + yib, (c / G_::YIB) & 1, a.status)) return false;
-  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(8 + ((r >> 5) == 3), c, 8);
+  if (!wait_bar(m, B_Y0 + yb, (c / G_::YB) & 1, a.status)) return false;
+  if (!wait_bar(m, B_YI0 + yib, (c / G_::YIB) & 1, a.status)) return false;
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 8);
   ptx::tc_fence_after();
+  // the previous chunk's bulk store must have read the staging buffer (long done by now)
+  if (c > 0) {
+    if (r == 0) {
+      ptx::bulk_wait_read();
+      ptx::mbar_arrive(&m->bar[OUT_READ]);
+    }
+    if (!wait_bar(m, OUT_READ, (c - 1) & 1, a.status)) return false;
+  }
   uint8_t* stage = sm + G_::OFF_S;
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
-    const int box = 2 * c + half;   // staged boxes so far
-    // the previous box's bulk store must have read the staging buffer
-    if (box > 0) {
-      if (r == 0) {
-        ptx::bulk_wait_read();
-        ptx::mbar_arrive(&m->bar[OUT_READ]);
-      }
-      if (!wait_barw(m, OUT_READ, (box - 1) & 1, a.status)) return false;
-    }
     float y[32], yi[32];
     ptx::tmem_ld32(tmem + COL_Y0 + 64 * yb + 32 * half, y);
     ptx::tmem_ld32(tmem + G_::COL_YI0 + 64 * yib + 32 * half, yi);
@@ -630,15 +596,6 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
       }
     }
     ptx::tmem_ld_wait();
-    if (half == 1) {
-      // both halves of Y and Yi have been read: MMA2 and MMA3 may reuse the buffers
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
-        ptx::mbar_arrive(&m->bar[YI_FREE0 + yib]);
-      }
-    }
 #pragma unroll
     for (int k = 0; k < 32; k += 2) {   // Y already holds D x (diagonal)
       const float2 o = ptx::fma2(make_float2(sdec, sdec), make_float2(yi[k], yi[k + 1]), make_float2(y[k], y[k + 1]));
@@ -658,25 +615,32 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
         y[2 * k + 1] *= silu_tanh(f.y);
       }
     }
+    uint8_t* box = stage + half * (QI * 128);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      *reinterpret_cast<float4*>(stage + ptx::sw128_off(r, k)) =
+      *reinterpret_cast<float4*>(box + ptx::sw128_off(r, k)) =
           make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[STAGED]);
-    if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(8 + ((r >> 5) == 3), c, 9);
-    if (r == 0) {
-      // all 128 rows of this 32-column box staged: one bulk store
-      if (!wait_barw(m, STAGED, box & 1, a.status)) return false;
-      ptx::tma_store_3d(&a.tm_out, stage, h * PT + 32 * half, sp.t0, bi);
-      ptx::bulk_commit();
-    }
   }
-  // A short chunk followed by more tokens (a packed sequence ending) also stored rows of
-  // the next chunk, which that chunk stores again: let this store land first.
-  if (r == 0 && sp.n < QI && sp.t0 + QI < a.L) ptx::bulk_wait_all();
-  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(8 + ((r >> 5) == 3), c, 10);
+  ptx::tc_fence_before();
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::mbar_arrive(&m->bar[Y_FREE0 + yb]);
+    ptx::mbar_arrive(&m->bar[YI_FREE0 + yib]);
+    ptx::mbar_arrive(&m->bar[STAGED]);
+  }
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 9);
+  if (r == 0) {
+    // all 128 rows staged: one bulk store per 32-column box
+    if (!wait_bar(m, STAGED, c & 1, a.status)) return false;
+    ptx::tma_store_3d(&a.tm_out, stage, h * PT, sp.t0, bi);
+    ptx::tma_store_3d(&a.tm_out, stage + QI * 128, h * PT + 32, sp.t0, bi);
+    ptx::bulk_commit();
+    // A short chunk followed by more tokens (a packed sequence ending) also stored rows of
+    // the next chunk, which that chunk stores again: let this store land first.
+    if (sp.n < QI && sp.t0 + QI < a.L) ptx::bulk_wait_all();
+  }
+  if ((r >> 5) == 0 || (r >> 5) == 3) TRACE(2 + ((r >> 5) == 3), c + 1, 10);
   return true;
 }
 
@@ -750,7 +714,7 @@ __device__ __forceinline__ void score_block_exact(const float (&v)[32], uint32_t
 // ---------------------------------------------------------------------------
 // score workers SA (warps 4-7, half 0) and SB (warps 8-11, half 1).  Both build score
 // column blocks {half, half+2} of the rows of their quadrant (quadrant q has q+1 non-zero
-// blocks, so no warp does more than two).
+// blocks, so no warp does more than two).  Each also builds half of xs first.
 // ---------------------------------------------------------------------------
 template <int NT, bool HAS_SEQ, bool HAS_Z>
 __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h, int half) {
@@ -761,28 +725,55 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
   const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
   const float dg = m->Dh;
   using G_ = Geo<NT>;
+  uint8_t* xs_sm = sm + G_::OFF_XS;
   const int nci = m->nci;
 #pragma unroll 1
   for (int c = 0; c < nci; ++c) {
-    const int buf = c & 1;
+    const int buf = c & 1, xb = c % G_::XST;
     const Span sp = span_at(a, c);
     const int64_t t0 = sp.t0;
     const int trole = 2 * half + (q == 3);
     (void)trole;
     if (q == 0 || q == 3) TRACE(trole, c, 0);
-    int seqv = (r < sp.n) ? 0 : -1, sl0 = 0, sl1 = 0;
+    int seqv = (r < sp.n) ? 0 : -1, end_seq = 0, sl0 = 0, sl1 = 0;
+    const int last_valid = sp.n - 1;
     if (has_seq) {
       seqv = (r < sp.n) ? seq_at(a, bi, t0 + r) : -1;
+      end_seq = seq_at(a, bi, t0 + last_valid);
       sl0 = seq_at(a, bi, t0 + half * 32 + lane);
       sl1 = seq_at(a, bi, t0 + (half + 2) * 32 + lane);
     }
-    if (!wait_barw(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
+    if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return;
     const float dA = m->dA[buf][r];
     if (q == 0 || q == 3) TRACE(trole, c, 2);
 
+    {
+      // ---- E1: xs[r] = x[r] * exp(dA_last - dA_r) dt_r  (chunk-end sequence only) -----
+      // SA writes head-dim columns 0-31, SB columns 32-63
+      // exp(dA_last - dA_r) dt_r, from w_r = exp(dA_{32q} - dA_r) dt_r in a factored block
+      const bool fq = block_factored(factor, m->dA[buf], q);
+      const float e1 = __expf(m->dA[buf][QI - 1] - (fq ? m->dA[buf][32 * q] : dA)) * m->dt[buf][r];
+      const float scale = (end_seq >= 0 && seqv == end_seq) ? e1 : 0.f;
+      if (!wait_bar(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return;
+      if (c > 0 && !wait_bar(m, XS_FREE, (c - 1) & 1, a.status)) return;   // MMA_L(c-1) done with xs
+      if (q == 0 || q == 3) TRACE(trole, c, 3);
+      const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
+#pragma unroll
+      for (int k = 4 * half; k < 4 * half + 4; ++k)
+        *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, k)) =
+            scale_row16(*reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, k)), scale);
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&m->bar[XS_FULL]);
+      if (q == 0 || q == 3) TRACE(trole, c, 8);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
+      if (q == 0 || q == 3) TRACE(trole, c, 4);
+    }
+
     // ---- E2: S[r][t] = CB[r][t] exp(dA_r - dA_t) dt_t  (t <= r, same sequence) ------
     const int cb = c & 1;
-    if (!wait_barw(m, B_CB0 + cb, (c >> 1) & 1, a.status)) return;
+    if (!wait_bar(m, B_CB0 + cb, (c >> 1) & 1, a.status)) return;
     if (q == 0 || q == 3) TRACE(trole, c, 6);
     ptx::tc_fence_after();
 #pragma unroll 1
@@ -837,33 +828,30 @@ __device__ void score_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
 
 // ---------------------------------------------------------------------------
 // state worker T (warps 12-15).  S_{c+1} = decay_c S_c + B^T xs_c, with the product added
-// by MMA_L(c) onto the state T has already scaled in TMEM.  Per chunk c, once MMA_L(c) and
-// MMA3(c) are done: read S_{c+1}, write its bf16 copy for MMA3(c+1) (and the varlen / final
-// state), store decay_{c+1} S_{c+1} back for MMA_L(c+1).  Thread r owns state rows
+// by MMA_L(c) onto the state T has already scaled in TMEM.  Per chunk c, once MMA_L(c) is
+// done: read S_{c+1}, write its bf16 copy for MMA3(c+1) (and the varlen / final state),
+// store decay_{c+1} S_{c+1} back for MMA_L(c+1); the output epilogue of c-1 runs before
+// (one Yi buffer) or after (two) that copy.  Thread r owns state rows
 // n = r + 128*hh (TMEM lane r, 64 f32 columns per 128-row half).  decay_c is 0 when the
 // chunk-end sequence id changes (state_passing_fwd.py:208-225; the id before the first
-// chunk counts as 0).  While MMA_L(c) and MMA3(c) run, T builds xs of chunk c+1 (E1) in the
-// other xs buffer, so MMA_L(c+1) waits only for the copy.  The output epilogue runs on its
-// own warpgroup (O).
+// chunk counts as 0).
 // ---------------------------------------------------------------------------
-// What T needs of chunk c's dA arrays, read as soon as they land (then released): the
-// chunk decay decay_c and the xs scale of row r, exp(dA_last - dA_r) dt_r for rows of the
-// chunk-end sequence (0 otherwise), from w_r = exp(dA_{32q} - dA_r) dt_r in a factored block.
-template <bool HAS_SEQ>
-__device__ __forceinline__ bool chunk_factors(const TcArgs& a, Misc* m, int bi, int c, int r, bool factor,
-                                              int& prev_end, float& decay, float& xscale) {
-  const int buf = c & 1, lane = r & 31, q = r >> 5;
+template <int NT, bool HAS_SEQ>
+__device__ __forceinline__ bool chunk_decay(const TcArgs& a, Misc* m, int bi, int c, int r, int& prev_end,
+                                            float& decay, float& sdec) {
+  const int buf = c & 1, lane = r & 31;
   const Span sp = span_at(a, c);
-  int end_seq = 0, seqv = r < sp.n ? 0 : -1;
+  const int end_seq = HAS_SEQ ? seq_at(a, bi, (int64_t)sp.t0 + sp.n - 1) : 0;
+  // row r continues the previous chunk's sequence: it reads the passed state (rule A9)
+  bool cont = r < sp.n;
   if (HAS_SEQ) {
-    end_seq = seq_at(a, bi, (int64_t)sp.t0 + sp.n - 1);
-    seqv = r < sp.n ? seq_at(a, bi, (int64_t)sp.t0 + r) : -1;
+    const int sr = seq_at(a, bi, (int64_t)sp.t0 + r);
+    const int sp0 = c == 0 ? 0 : seq_at(a, bi, (int64_t)sp.t0 - 1);
+    cont = cont && sr == sp0;
   }
-  if (!wait_barw(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return false;
-  const float* dA = m->dA[buf];
-  const float dA_last = dA[QI - 1];
-  const float e1 = __expf(dA_last - w_ref(factor, dA, r)) * m->dt[buf][r];
-  xscale = (end_seq >= 0 && seqv == end_seq) ? e1 : 0.f;
+  if (!wait_bar(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) return false;
+  const float dA_last = m->dA[buf][QI - 1];
+  sdec = cont ? __expf(m->dA[buf][r]) : 0.f;
   __syncwarp();
   if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
   decay = (end_seq == prev_end) ? __expf(dA_last) : 0.f;
@@ -871,49 +859,23 @@ __device__ __forceinline__ bool chunk_factors(const TcArgs& a, Misc* m, int bi, 
   return true;
 }
 
-// E1 for chunk c: xs[r] = x[r] * xscale (all 64 head-dim columns of row r) into xs buffer
-// c % 2, once x(c) has landed (MMA_L(c-2), the buffer's last reader, is done); then xs is
-// handed to MMA_L(c) and T's share of the x tile is released.
-template <int NT>
-__device__ __forceinline__ bool build_xs(const TcArgs& a, uint8_t* sm, Misc* m, int c, int r, float xscale) {
-  using G_ = Geo<NT>;
-  const int xb = c % G_::XST, lane = r & 31;
-  if (!wait_barw(m, X_FULL0 + xb, (c / G_::XST) & 1, a.status)) return false;
-  const uint8_t* x_sm = sm + G_::OFF_X + xb * G_::SZ_X;
-  uint8_t* xs_sm = sm + G_::OFF_XS + (c & 1) * G_::SZ_X;
-  uint4 w[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) w[k] = *reinterpret_cast<const uint4*>(x_sm + ptx::sw128_off(r, k));
-#pragma unroll
-  for (int k = 0; k < 8; ++k) *reinterpret_cast<uint4*>(xs_sm + ptx::sw128_off(r, k)) = scale_row16(w[k], xscale);
-  ptx::fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    ptx::mbar_arrive(&m->bar[XS_FULL0 + (c & 1)]);
-    ptx::mbar_arrive(&m->bar[X_EMPTY0 + xb]);
-  }
-  return true;
-}
-
-template <int NT, bool HAS_SEQ>
+template <int NT, bool HAS_SEQ, bool HAS_Z>
 __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
   using G_ = Geo<NT>;
   const int r = threadIdx.x & 127;
   const int q = r >> 5, lane = r & 31;
   const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
   uint8_t* st_sm = sm + G_::OFF_ST;
-  const int64_t bh = (int64_t)bi * a.H + h;
   // with a split sequence, row bi is segment bi % seg_k of batch row bi / seg_k: only the
   // last segment's state is a final state
   const int64_t ib = bi / a.seg_k, fbh = ib * a.H + h;
   const int jseg = bi % a.seg_k;
-  float* const fin = (bi % a.seg_k == a.seg_k - 1) ? a.final_states : nullptr;
+  float* const fin = (jseg == a.seg_k - 1) ? a.final_states : nullptr;
   const int nci = m->nci;
   if (nci <= 0) return;
-  const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);   // dA non-increasing
   int prev_end = 0;
-  float decay, xscale, decay_next = 0.f, xscale_next = 0.f;
-  if (!chunk_factors<HAS_SEQ>(a, m, bi, 0, r, factor, prev_end, decay, xscale)) return;
+  float decay, sd_cur, sd_next = 0.f, sd_prev = 0.f;   // per-row inter-chunk factors of c, c+1, c-1
+  if (!chunk_decay<NT, HAS_SEQ>(a, m, bi, 0, r, prev_end, decay, sd_cur)) return;
   // S_0 = initial state (or 0): bf16 operand for MMA3(0); decay_0 S_0 in TMEM for MMA_L(0)
 #pragma unroll 1
   for (int seg = 0; seg < 2 * G_::NH; ++seg) {
@@ -955,7 +917,6 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     ptx::mbar_arrive(&m->bar[ST_READY]);
     ptx::mbar_arrive(&m->bar[SCALED]);
   }
-  if (!build_xs<NT>(a, sm, m, 0, r, xscale)) return;
 
 #pragma unroll 1
   for (int c = 0; c < nci; ++c) {
@@ -965,12 +926,11 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     const Span sp = span_at(a, c);
     float* const vdst = sp.vslot >= 0 ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
     TRACE(5, c, 0);
-    // xs of chunk c+1 into the other xs buffer (MMA_L(c-1), its last reader, is done: B_L(c-1))
-    if (more && !chunk_factors<HAS_SEQ>(a, m, bi, c + 1, r, factor, prev_end, decay_next, xscale_next)) return;
-    if (more && !build_xs<NT>(a, sm, m, c + 1, r, xscale_next)) return;
-    TRACE(5, c, 3);
-    // S_{c+1} ready (MMA_L(c)); MMA3(c) done with the bf16 copy of S_c
-    if (!wait_barw(m, B_L, c & 1, a.status)) return;
+    if (more && !chunk_decay<NT, HAS_SEQ>(a, m, bi, c + 1, r, prev_end, decay, sd_next)) return;
+    // With one Yi buffer MMA3(c) writes Yi after the output of c-1 has read it, so that
+    // output comes first; with two it follows the state copy, overlapping MMA3/MMA_L(c+1).
+    if (G_::YIB == 1 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
+    if (!wait_bar(m, B_L, c & 1, a.status)) return;   // S_{c+1} ready, MMA3(c) done with the copy of S_c
     TRACE(5, c, 1);
     ptx::tc_fence_after();
 #pragma unroll 1
@@ -992,7 +952,7 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
                          pack_bf16(sv[8 * j + 4], sv[8 * j + 5]), pack_bf16(sv[8 * j + 6], sv[8 * j + 7]));
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float2 d2 = ptx::mul2(make_float2(sv[i], sv[i + 1]), make_float2(decay_next, decay_next));
+          const float2 d2 = ptx::mul2(make_float2(sv[i], sv[i + 1]), make_float2(decay, decay));
           sv[i] = d2.x;
           sv[i + 1] = d2.y;
         }
@@ -1013,38 +973,11 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
       }
     }
     TRACE(5, c, 2);
+    if (G_::YIB == 2 && c > 0 && !output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c - 1, r, sd_prev)) return;
+    sd_prev = sd_cur;
+    sd_cur = sd_next;
   }
-}
-
-// ---------------------------------------------------------------------------
-// output worker O (warps 16-19): the epilogue E4 of every chunk, out = Y + sdec Yi (z gate),
-// as soon as MMA2(c) and MMA3(c) are done.  sdec_r = exp(dA_r) when row r continues the
-// sequence of the previous chunk (it reads the passed state, rule A9), else 0.  Thread r
-// owns output row r of each chunk (TMEM lane r).
-// ---------------------------------------------------------------------------
-template <int NT, bool HAS_SEQ, bool HAS_Z>
-__device__ void output_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int h) {
-  const int r = threadIdx.x & 127;
-  const int q = r >> 5, lane = r & 31;
-  const uint32_t tl = m->tmem_base + ((uint32_t)(q * 32) << 16);
-  const int nci = m->nci;
-#pragma unroll 1
-  for (int c = 0; c < nci; ++c) {
-    const int buf = c & 1;
-    const Span sp = span_at(a, c);
-    bool cont = r < sp.n;
-    if (HAS_SEQ) {
-      const int sr = seq_at(a, bi, (int64_t)sp.t0 + r);
-      const int sp0 = c == 0 ? 0 : seq_at(a, bi, (int64_t)sp.t0 - 1);
-      cont = cont && sr == sp0;
-    }
-    if (q == 0 || q == 3) TRACE(8 + (q == 3), c, 0);
-    if (!wait_barw(m, DA_READY0 + buf, (c >> 1) & 1, a.status)) break;
-    const float sdec = cont ? __expf(m->dA[buf][r]) : 0.f;
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&m->bar[DA_FREE0 + buf]);
-    if (!output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, c, r, sdec)) break;
-  }
+  if (!output_chunk<NT, HAS_Z>(a, sm, m, tl, bi, h, nci - 1, r, sd_prev)) return;
   if (r == 0) ptx::bulk_wait_all();   // every bulk store of this CTA has landed
 }
 
@@ -1074,17 +1007,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     ptx::mbar_init(&m->bar[X_EMPTY1], X_EMPTY_COUNT);
     ptx::mbar_init(&m->bar[CB_FREE0], 8);    // SA and SB done with the CB buffer
     ptx::mbar_init(&m->bar[CB_FREE1], 8);
-    ptx::mbar_init(&m->bar[XS_FULL0], 4);    // T: xs built (per xs buffer)
-    ptx::mbar_init(&m->bar[XS_FULL1], 4);
+    ptx::mbar_init(&m->bar[XS_FULL], 8);     // SA and SB: their halves of xs
     ptx::mbar_init(&m->bar[S_FULL_A0], 8);   // SA and SB: score blocks 0, 1
     ptx::mbar_init(&m->bar[S_FULL_A1], 8);
     ptx::mbar_init(&m->bar[S_FULL_B0], 8);   // SA and SB: score blocks 2, 3
     ptx::mbar_init(&m->bar[S_FULL_B1], 8);
     ptx::mbar_init(&m->bar[ST_READY], 4);    // T: bf16 state copy for MMA3
     ptx::mbar_init(&m->bar[SCALED], 4);      // T: TMEM state scaled by the chunk decay
-    ptx::mbar_init(&m->bar[Y_FREE0], 4);     // O: output read Y
+    ptx::mbar_init(&m->bar[Y_FREE0], 4);     // T: output read Y
     ptx::mbar_init(&m->bar[Y_FREE1], 4);
-    ptx::mbar_init(&m->bar[YI_FREE0], 4);    // O: output read Yi
+    ptx::mbar_init(&m->bar[YI_FREE0], 4);    // T: output read Yi
     ptx::mbar_init(&m->bar[YI_FREE1], 4);
     ptx::mbar_init(&m->bar[DA_FREE0], DA_FREE_COUNT);
     ptx::mbar_init(&m->bar[DA_FREE1], DA_FREE_COUNT);
@@ -1096,10 +1028,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
   }
 #ifdef SSD_TC_DEBUG_TRACE
   if (a.trace && threadIdx.x == 0 && blockIdx.x < 2048) {
-    a.trace[TRACE_ROLES * 64 * 16 + 3 * blockIdx.x] = ptx::globaltimer();
+    a.trace[8 * 64 * 16 + 3 * blockIdx.x] = ptx::globaltimer();
     unsigned smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    a.trace[TRACE_ROLES * 64 * 16 + 3 * blockIdx.x + 2] = smid;
+    a.trace[8 * 64 * 16 + 3 * blockIdx.x + 2] = smid;
   }
 #endif
   if (threadIdx.x == 0) m->Dh = a.D_ndim == 1 ? a.D[h] : 0.f;
@@ -1134,36 +1066,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_fused_tc_kernel(const __grid_
     }
     __syncthreads();
   }
-  // Each warpgroup sets its register budget at the top of its own branch, so that no code
-  // after a setmaxnreg is shared between budgets.  A CTA whose test-mode wait gave up skips
-  // its work (nothing has been issued).
-  if (warp < 4) {
-    ptx::setmaxnreg_dec<role_regs<NT>()>();
-    if (m->abort) {
-    } else if (warp == W_PRODUCER) {
-      if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
-    } else if (warp == W_ISSUE_A) {
-      if (lane == 0) mma_issuer_a<NT>(a, sm, m);
-    } else if (warp == W_DA) {
-      if (lane == 0) da_producer(a, m, bi, h);
-    } else {
-      if (lane == 0) mma_issuer_b<NT>(a, sm, m);
-    }
+  if (m->abort) {
+    // nothing issued: fall through to the TMEM release
+  } else if (warp == W_PRODUCER) {
+    if (lane == 0) producer<NT>(a, sm, m, bi, h, g);
+  } else if (warp == W_ISSUE_A) {
+    if (lane == 0) mma_issuer_a<NT>(a, sm, m);
+  } else if (warp == W_DA) {
+    if (lane == 0) da_producer(a, m, bi, h);
+  } else if (warp == W_ISSUE_B) {
+    if (lane == 0) mma_issuer_b<NT>(a, sm, m);
+  } else if (warp < 12) {
+    score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
   } else {
-    ptx::setmaxnreg_inc<WORKER_REGS>();
-    if (m->abort) {
-    } else if (warp < 12) {
-      score_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h, (warp - 4) >> 2);
-    } else if (warp < 16) {
-      state_worker<NT, HAS_SEQ>(a, sm, m, bi, h);
-    } else {
-      output_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h);
-    }
+    state_worker<NT, HAS_SEQ, HAS_Z>(a, sm, m, bi, h);
   }
   ptx::tc_fence_before();
   __syncthreads();
 #ifdef SSD_TC_DEBUG_TRACE
-  if (a.trace && threadIdx.x == 0 && blockIdx.x < 2048) a.trace[TRACE_ROLES * 64 * 16 + 3 * blockIdx.x + 1] = ptx::globaltimer();
+  if (a.trace && threadIdx.x == 0 && blockIdx.x < 2048) a.trace[8 * 64 * 16 + 3 * blockIdx.x + 1] = ptx::globaltimer();
 #endif
   if (warp == 1) {
     ptx::tc_fence_after();
@@ -1317,7 +1238,7 @@ __device__ __forceinline__ bool seg_wait(uint64_t* bar, uint32_t parity, unsigne
   const long long t0 = clock64();
   while (!ptx::mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > TIMEOUT_CYCLES) {
-      atomicCAS(status, 0u, (unsigned)(0x100 | id));
+      if (status) atomicCAS(status, 0u, (unsigned)(0x100 | id));
       return false;
     }
   }
@@ -1461,6 +1382,154 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
 
 
 // ---------------------------------------------------------------------------
+// Sequence-parallel decay fix-up on the tensor cores (bf16 C, P = 64, N = 128 or 256).
+// For every token t of the carried sequence, out[t] += exp(dA(t)) (C_t . S^T) (silu(z_t)),
+// the inter-chunk term of chunk_scan_fwd.py:108-232 with the received state S: per
+// 128-token tile one tcgen05 product Y = C_tile . S^T (M = 128 tokens, N = 64, K = dstate;
+// A = the C tile by TMA, B = S as bf16 [n][p] in shared memory, as the fused kernel's MMA3),
+// then each thread adds its token's row.  dA(t) is the segment-wide cumulative dt*A: the
+// chunk totals before t's chunk plus the within-chunk value, from the (b, H, nc, Q)
+// chunk_cumsum output.  The extra x-block updates the final state.
+// ---------------------------------------------------------------------------
+struct FixArgs {
+  CUtensorMap tm_c;
+  int64_t L, H, G, Q, nc;
+  const float* dA;
+  const float* S;
+  const int32_t* carried;
+  const bf16* z;
+  float* out;
+  float* final_states;
+  unsigned* status;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(128) tc_sp_fixup_kernel(const __grid_constant__ FixArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr uint32_t SZ_C = QI * NT * 2, OFF_ST = SZ_C;
+  __shared__ uint64_t full, done;
+  __shared__ uint32_t tbase;
+  __shared__ float base_dA;
+  const int r = threadIdx.x, warp = r >> 5, lane = r & 31;
+  const int64_t bi = blockIdx.z, h = blockIdx.y;
+  const int64_t ntiles = (a.L + QI - 1) / QI;
+  const int64_t clen = a.carried ? min((int64_t)a.carried[bi], a.L) : a.L;
+  const float* dAh = a.dA + (bi * a.H + h) * a.nc * a.Q;
+  const float* Sh = a.S + (bi * a.H + h) * PT * NT;
+  if (blockIdx.x == ntiles) {   // final state: += exp(total dA) S when the carried sequence reaches the end
+    if (a.final_states == nullptr || clen < a.L) return;
+    float part = 0.f;
+    for (int64_t c = r; c < a.nc; c += 128) part += dAh[c * a.Q + a.Q - 1];
+    __shared__ float red[4];
+    part = warp_sum(part);
+    if (lane == 0) red[warp] = part;
+    __syncthreads();
+    const float dec = __expf(red[0] + red[1] + red[2] + red[3]);
+    float* fh = a.final_states + (bi * a.H + h) * PT * NT;
+    for (int64_t i = r; i < PT * NT; i += 128) fh[i] = fmaf(dec, Sh[i], fh[i]);
+    return;
+  }
+  const int64_t t0 = (int64_t)blockIdx.x * QI;
+  if (t0 >= clen) return;
+  const int g = (int)(h / (a.H / a.G));
+  if (r == 0) {
+    ptx::mbar_init(&full, 1);
+    ptx::mbar_init(&done, 1);
+    ptx::fence_mbar_init();
+    ptx::mbar_arrive_expect_tx(&full, SZ_C);
+    for (int j = 0; j < NT / 64; ++j) ptx::tma_load_3d(sm + j * (QI * 128), &a.tm_c, &full, g * NT + 64 * j, (int)t0, (int)bi);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(&tbase, 64);
+    ptx::tmem_relinquish();
+    // chunk totals before t0's chunk
+    const int64_t c0 = t0 / a.Q;
+    float part = 0.f;
+    for (int64_t c = lane; c < c0; c += 32) part += dAh[c * a.Q + a.Q - 1];
+    part = warp_sum(part);
+    if (lane == 0) base_dA = part;
+  }
+  // S as bf16 [n][p] (128-byte rows, swizzled): thread r owns rows n = r + 128 hh
+  uint8_t* st_sm = sm + OFF_ST;
+  for (int hh = 0; hh < NT / 128; ++hh) {
+    const int n = hh * 128 + r;
+    for (int half = 0; half < 2; ++half) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = Sh[(int64_t)(32 * half + i) * NT + n];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(st_sm + ptx::sw128_off(n, 4 * half + j)) =
+            make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                       pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+    }
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  bool ok = true;
+  if (r == 0) {
+    if (seg_wait(&full, 0, a.status, 6)) {
+      constexpr uint32_t ID = ptx::idesc_bf16_f32(128, 64, 0, 1);
+      const uint32_t base = ptx::smem_u32(sm);
+      for (int hh = 0; hh < NT / 128; ++hh) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t offa = hh * (QI * 256) + (i >> 2) * (QI * 128) + (i & 3) * 32;
+          ptx::mma_f16(tbase, ptx::sdesc_sw128(base + offa, 16, 1024),
+                       ptx::sdesc_sw128(base + OFF_ST + hh * (128 * 128) + i * 2048, 8192, 1024), ID,
+                       (hh > 0 || i > 0) ? 1u : 0u);
+        }
+      }
+    }
+    ptx::mma_commit(&done);
+  }
+  // this thread's token: its decay while the MMA runs
+  const int64_t t = t0 + r;
+  float dg = 0.f;
+  if (t < clen) {
+    const int64_t c = t / a.Q;
+    float run = base_dA;
+    for (int64_t cc = t0 / a.Q; cc < c; ++cc) run += dAh[cc * a.Q + a.Q - 1];
+    dg = __expf(run + dAh[c * a.Q + (t - c * a.Q)]);
+  }
+  ok = seg_wait(&done, 0, a.status, 7);
+  ptx::tc_fence_after();
+  if (ok) {
+    for (int half = 0; half < 2; ++half) {
+      float y[32];
+      ptx::tmem_ld32(tbase + ((uint32_t)(warp * 32) << 16) + 32 * half, y);
+      ptx::tmem_ld_wait();
+      if (t < clen) {
+        const int64_t row = ((bi * a.L + t) * a.H + h) * PT + 32 * half;
+        float4* o = reinterpret_cast<float4*>(a.out + row);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float4 v = o[k];
+          float f[4] = {dg * y[4 * k], dg * y[4 * k + 1], dg * y[4 * k + 2], dg * y[4 * k + 3]};
+          if (a.z) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) f[e] *= silu(__bfloat162float(a.z[row + 4 * k + e]));
+          }
+          v.x += f[0]; v.y += f[1]; v.z += f[2]; v.w += f[3];
+          o[k] = v;
+        }
+      }
+    }
+  } else if (r == 0) {
+    seg_wait(&full, 0, a.status, 8);   // never leave with the copy still landing
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, 64);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1567,8 +1636,7 @@ size_t seg_bytes(const ssd_fwd_params_t* p) {
 }
 
 size_t tc_workspace_bytes(const ssd_fwd_params_t* p) {
-  return tc_supported(p) ? sched_bytes(p) + prep_bytes(p) + seg_bytes(p) +
-                               (trace_enabled() ? TRACE_ROLES * 64 * 16 * 8 + 3 * 8 * 2048 : 0)
+  return tc_supported(p) ? sched_bytes(p) + prep_bytes(p) + seg_bytes(p) + (trace_enabled() ? 8 * 64 * 16 * 8 + 65536 : 0)
                          : 0;
 }
 
@@ -1584,16 +1652,46 @@ bool ensure_smem_attr(void (*kern)(TcArgs), int kid) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < kMaxDev && (done[dev] >> kid & 1)) return true;
-  // The warpgroups' setmaxnreg split assumes the block launches with exactly LAUNCH_REGS
-  // registers per thread; with fewer, an increment would wait for ever.  Refuse instead.
-  cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != LAUNCH_REGS ||
-      fa.maxThreadsPerBlock < NTHREADS)
-    return false;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LAUNCH_BYTES) != cudaSuccess)
     return false;
   if (dev >= 0 && dev < kMaxDev) done[dev] |= (uint8_t)(1u << kid);
   return true;
+}
+
+bool tc_sp_fixup_supported(const ssd_sp_fixup_params_t* p) {
+  return p->dtype == SSD_DTYPE_BF16 && p->headdim == PT && (p->dstate == 128 || p->dstate == 256) &&
+         !(reinterpret_cast<uintptr_t>(p->C) & 15) && !(reinterpret_cast<uintptr_t>(p->out) & 15) &&
+         p->batch * p->nheads <= 65535 && p->seqlen < 0x7fffffff && encode_fn() != nullptr;
+}
+
+int tc_sp_fixup(const ssd_sp_fixup_params_t* p, cudaStream_t st) {
+  FixArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!make_map(&a.tm_c, p->C, (uint64_t)p->ngroups * p->dstate, p->seqlen, p->batch)) {
+    set_last_error("cuTensorMapEncodeTiled failed for C");
+    return SSD_ERR_CUDA;
+  }
+  a.L = p->seqlen; a.H = p->nheads; a.G = p->ngroups; a.Q = p->chunk_size;
+  a.nc = (p->seqlen + p->chunk_size - 1) / p->chunk_size;
+  a.dA = p->dA_cumsum; a.S = p->state_in; a.carried = p->carried_len; a.z = (const bf16*)p->z;
+  a.out = p->out; a.final_states = p->final_states;
+  a.status = nullptr;   // no workspace: a wait that gives up leaves that tile's tokens without the update
+  const dim3 grid((unsigned)((p->seqlen + QI - 1) / QI + 1), (unsigned)p->nheads, (unsigned)p->batch);
+  if (p->dstate == 256) {
+    const uint32_t bytes = QI * 256 * 2 + 256 * PT * 2 + 1024;
+    cudaFuncSetAttribute(tc_sp_fixup_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    tc_sp_fixup_kernel<256><<<grid, 128, bytes, st>>>(a);
+  } else {
+    const uint32_t bytes = QI * 128 * 2 + 128 * PT * 2 + 1024;
+    cudaFuncSetAttribute(tc_sp_fixup_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    tc_sp_fixup_kernel<128><<<grid, 128, bytes, st>>>(a);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error(cudaGetErrorString(e));
+    return SSD_ERR_CUDA;
+  }
+  return SSD_OK;
 }
 
 int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace, cudaStream_t st) {
@@ -1632,8 +1730,7 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
   const int kid = (p->dstate == 256 ? 4 : 0) + (p->seq_idx ? 2 : 0) + (p->z ? 1 : 0);
   const KernelFn kern = kernels[kid];
   if (!ensure_smem_attr(kern, kid)) {
-    set_last_error("fused kernel set-up failed: its register count is not the one its warpgroup split "
-                   "assumes, or cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
+    set_last_error("cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
     return SSD_ERR_CUDA;
   }
   if (p->varlen_states) {

@@ -17,4 +17,8 @@ int tc_num_launches(const ssd_fwd_params_t* p);
 // word (cleared by the caller on the stream); a bounded wait that gives up writes there.
 int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace, cudaStream_t st);
 
+// The sequence-parallel fix-up on the tensor cores (bf16 C, P = 64, N = 128 or 256).
+bool tc_sp_fixup_supported(const ssd_sp_fixup_params_t* p);
+int tc_sp_fixup(const ssd_sp_fixup_params_t* p, cudaStream_t st);
+
 }  // namespace ssd
