@@ -887,6 +887,9 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     // S_j = sum_{l<j} exp(total dA of segments l+1..j-1) L_l + exp(total dA of 0..j-1) S_init
     // (segment j = bi % seg_k of batch row bi / seg_k; without a split j = 0, S_0 = S_init)
     float sdA = 0.f;
+    // the segment-state pass may still be running (this kernel is its programmatic
+    // dependent): wait for its results before the first read
+    if (jseg > 0 && seg == 0) ptx::griddep_wait();
     for (int l = jseg - 1; l >= 0; --l) {
       const int64_t lr = (ib * a.seg_k + l) * a.H + h;
       const float coef = __expf(sdA);
@@ -1299,6 +1302,8 @@ __global__ void __launch_bounds__(128, 1) tc_segstate_kernel(const __grid_consta
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  // the fused kernel may start now: its CTAs read this pass's results only after waiting
+  ptx::griddep_launch_dependents();
   if (r == 0)
     for (int c = 0; c < nc && c < ST; ++c) seg_load<NT>(a, sm + c * G_::SZ_STAGE, &full[c], g, h, c, row);
   const bool factor = (a.A[h] <= 0.f) && (a.lo >= 0.f);
@@ -1775,7 +1780,24 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
     a.seg_state = seg_state;
     a.seg_tot = sa.seg_tot;
   }
-  kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
+  if (k > 1) {
+    // a programmatic dependent of the segment-state pass: its prologue, loads and
+    // intra-chunk work overlap that pass; the state warps wait for its results
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)(b * H));
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = SMEM_LAUNCH_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, a);
+  } else {
+    kern<<<(unsigned)(b * H), NTHREADS, SMEM_LAUNCH_BYTES, st>>>(a);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     char msg[160];
