@@ -1619,8 +1619,13 @@ size_t sched_bytes(const ssd_fwd_params_t* p) {
 int seg_split(const ssd_fwd_params_t* p) {
   if (p->seq_idx || p->varlen_states || p->seqlen % QI) return 1;
   const int64_t bh = p->batch * p->nheads, nci = p->seqlen / QI;
-  if (bh >= 96) return 1;
-  int k = (int)std::min<int64_t>(148 / bh, nci / 2);
+  // SSD_TC_SEGMENTS=k (tuning experiments only) forces the segment count
+  static const int forced = [] {
+    const char* e = getenv("SSD_TC_SEGMENTS");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 0 && bh >= 96) return 1;
+  int k = forced > 0 ? (int)std::min<int64_t>(forced, nci / 2) : (int)std::min<int64_t>(148 / bh, nci / 2);
   while (k > 1 && (nci % k || nci / k > 64)) --k;
   return std::max(k, 1);
 }
