@@ -1,6 +1,6 @@
 """Build libssd_b200.so (CUDA kernels + C ABI) in-tree for sm_100a with nvcc.
 
-Usage: python build.py [--force]
+Usage: python build.py [--force] [--debug]
 Each .cu file compiles to an object in _build/ (in parallel), then one shared library
 is linked into mamba2_b200/libssd_b200.so.  Rebuilds only when a source or header is
 newer than the library.
@@ -19,6 +19,9 @@ CSRC = HERE / "csrc"
 INCLUDE = REPO / "include"
 BUILD = HERE / "_build"
 LIB = HERE / "mamba2_b200" / "libssd_b200.so"
+# SSD_DEBUG variant: every global index of the fused kernel checked, out-of-range accesses
+# skipped and reported through the device status word
+LIB_DEBUG = HERE / "mamba2_b200" / "libssd_b200_debug.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--use_fast_math",
@@ -30,17 +33,17 @@ def _sources():
     return sorted(CSRC.glob("*.cu"))
 
 
-def _stale() -> bool:
-    if not LIB.exists():
+def _stale(lib=LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     deps = list(CSRC.glob("*")) + list(INCLUDE.glob("*.h")) + [pathlib.Path(__file__)]
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def _compile(src: pathlib.Path) -> pathlib.Path:
-    obj = BUILD / (src.stem + ".o")
-    cmd = [NVCC, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+def _compile(src: pathlib.Path, debug: bool = False) -> pathlib.Path:
+    obj = (BUILD / "debug" if debug else BUILD) / (src.stem + ".o")
+    cmd = [NVCC, *ARCH, *FLAGS, *(["-DSSD_DEBUG"] if debug else []), "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stdout}\n{r.stderr}")
@@ -49,18 +52,19 @@ def _compile(src: pathlib.Path) -> pathlib.Path:
     return obj
 
 
-def build(force: bool = False) -> pathlib.Path:
-    if not force and not _stale():
-        return LIB
-    BUILD.mkdir(exist_ok=True)
+def build(force: bool = False, debug: bool = False) -> pathlib.Path:
+    lib = LIB_DEBUG if debug else LIB
+    if not force and not _stale(lib):
+        return lib
+    (BUILD / "debug" if debug else BUILD).mkdir(parents=True, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
-        objs = list(ex.map(_compile, _sources()))
-    cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda"]
+        objs = list(ex.map(lambda src: _compile(src, debug), _sources()))
+    cmd = [NVCC, *ARCH, "-shared", "-o", str(lib), *map(str, objs), "-lcuda"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv))
+    print(build(force="--force" in sys.argv, debug="--debug" in sys.argv))

@@ -186,6 +186,9 @@ int ssd_status_decode(uint32_t word) {
   if ((word & ~0xffu) == 0x100u)
     return fail(SSD_ERR_TIMEOUT, "a bounded wait of the fused kernel gave up (barrier %u); the launch's outputs "
                 "are incomplete", word & 0xffu);
+  if ((word & ~0xffu) == 0x300u)
+    return fail(SSD_ERR_INVALID_ARG, "debug build: the fused kernel computed an out-of-range index (site %u) and "
+                "skipped that access", word & 0xffu);
   if (word == 0x200u)
     return fail(SSD_ERR_ALIGNMENT, "the fused kernel's dynamic shared memory window was not 1024-byte alignable; "
                 "the launch did no work");

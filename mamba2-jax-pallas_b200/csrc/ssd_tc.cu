@@ -155,6 +155,9 @@ struct TcArgs {
   unsigned* status;
   long long test_wait_cycles;  // > 0: test mode, see the start of ssd_fused_tc_kernel
   int seg_k;                   // rows per batch row when the sequence is split (1: no split)
+  int rows;                    // batch rows of the walk (b * seg_k)
+  int num_seqs;                // varlen states: sequences
+  int sched_cap;               // varlen: schedule entries (without the sentinel)
   const float* seg_state;      // split: L_j of every segment but the last, (b*seg_k, H, P, N)
   const float* seg_tot;        // split: total dA of each segment, (b*seg_k, H)
   unsigned long long* trace;   // debug phase timestamps (CTA 0, SSD_TC_TRACE=1), or null
@@ -178,6 +181,21 @@ struct TcArgs {
 // normal launch takes well under 1 ms.  The cycle counter is cheap to read, the global
 // timer is not.
 constexpr long long TIMEOUT_CYCLES = 4000000000LL;
+
+// SSD_DEBUG builds (build.py --debug, libssd_b200_debug.so) check every global index the
+// fused kernel computes against its tensor's extent; an index out of range is not accessed
+// and the status word records 0x300 | site (ssd_status_decode reports it).  Release builds
+// compile the checks away.
+#ifdef SSD_DEBUG
+__device__ __noinline__ bool dbg_fail(unsigned* status, int site) {
+  atomicCAS(status, 0u, 0x300u | (unsigned)site);
+  return false;
+}
+#define DBG_IN(idx, n, site) \
+  (((int64_t)(idx) >= 0 && (int64_t)(idx) < (int64_t)(n)) ? true : dbg_fail(a.status, (site)))
+#else
+#define DBG_IN(idx, n, site) true
+#endif
 
 // Bounded wait.  Returns false (after flagging the CTA and the status word) on timeout or
 // when another role of this CTA already gave up.  One probe is inlined; the spin loop is
@@ -232,10 +250,11 @@ struct Span {
 __device__ __forceinline__ Span span_at(const TcArgs& a, int c) {
   Span s;
   if (a.sched) {
-    const int2 e = a.sched[c];
+    const bool ok = DBG_IN(c + 1, a.sched_cap + 1, 1);
+    const int2 e = ok ? a.sched[c] : make_int2(0, -1);
     s.t0 = e.x;
     s.vslot = e.y;
-    s.n = a.sched[c + 1].x - e.x;
+    s.n = (ok ? a.sched[c + 1].x : e.x) - e.x;
   } else {
     s.t0 = c * QI;
     s.n = min(QI, a.L - s.t0);
@@ -298,7 +317,9 @@ __device__ void da_producer(const TcArgs& a, Misc* m, int bi, int h) {
   for (; c < nci; ++c) {
     const int buf = c & 1;
     if (c >= 2 && !wait_bar(m, DA_FREE0 + buf, ((c >> 1) - 1) & 1, a.status)) break;
-    const float* src = a.dtprep + (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
+    const int64_t si = (((int64_t)bi * a.H + h) * a.prep_cap + c) * (2 * QI);
+    if (!DBG_IN(si + 2 * QI - 1, (int64_t)a.rows * a.H * a.prep_cap * 2 * QI, 2)) break;
+    const float* src = a.dtprep + si;
     ptx::mbar_arrive_expect_tx(&m->bar[DA_READY0 + buf], 2 * QI * 4);
     ptx::bulk_load(m->dA[buf], src, QI * 4, &m->bar[DA_READY0 + buf]);
     ptx::bulk_load(m->dt[buf], src + QI, QI * 4, &m->bar[DA_READY0 + buf]);
@@ -476,7 +497,8 @@ __device__ __forceinline__ float load_dt(const TcArgs& a, int bi, int h, int nci
 }
 
 __device__ __forceinline__ int seq_at(const TcArgs& a, int bi, int64_t pos) {
-  return (pos < a.L) ? a.seq_idx[(int64_t)bi * a.L + pos] : -1;
+  return (pos < a.L && DBG_IN((int64_t)bi * a.L + pos, (int64_t)a.rows * a.L, 3)) ? a.seq_idx[(int64_t)bi * a.L + pos]
+                                                                               : -1;
 }
 
 // 16-byte word of 8 bf16, scaled by `s`, repacked.
@@ -565,7 +587,8 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
   // never stored) and issued before the waits so its latency overlaps them
   uint4 zq[8];
   if (HAS_Z) {
-    const uint4* const zp = reinterpret_cast<const uint4*>(a.z + o0);
+    const bool zok = DBG_IN(o0 + PT - 1, (int64_t)a.rows * a.L * a.H * PT, 4);
+    const uint4* const zp = reinterpret_cast<const uint4*>(a.z + (zok ? o0 : 0));
 #pragma unroll
     for (int k = 0; k < 8; ++k) zq[k] = __ldg(zp + k);
   }
@@ -603,7 +626,7 @@ __device__ bool output_chunk(const TcArgs& a, uint8_t* sm, Misc* m, uint32_t tme
       y[k + 1] = o.y;
     }
     if (HAS_Z) {
-      if (out_x != nullptr && valid) {
+      if (out_x != nullptr && valid && DBG_IN(o0 + PT - 1, (int64_t)a.rows * a.L * a.H * PT, 5)) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(out_x + o0 + 32 * half + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
@@ -892,13 +915,14 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     if (jseg > 0 && seg == 0) ptx::griddep_wait();
     for (int l = jseg - 1; l >= 0; --l) {
       const int64_t lr = (ib * a.seg_k + l) * a.H + h;
+      if (!DBG_IN(lr * PT * NT + (int64_t)(32 * half + 31) * NT + n, (int64_t)a.rows * a.H * PT * NT, 6)) break;
       const float coef = __expf(sdA);
       const float* Ll = a.seg_state + lr * PT * NT + n;
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmaf(coef, __ldcg(Ll + (32 * half + i) * NT), v[i]);
       sdA += __ldcg(a.seg_tot + lr);
     }
-    if (a.init) {
+    if (a.init && DBG_IN(((ib * a.H + h) * PT + 32 * half + 31) * NT + n, (int64_t)(a.rows / a.seg_k) * a.H * PT * NT, 7)) {
       const float coef = __expf(sdA);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmaf(coef, a.init[((ib * a.H + h) * PT + 32 * half + i) * NT + n], v[i]);
@@ -927,7 +951,8 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
     // this chunk ends packed sequence sp.vslot: the state after it is that sequence's
     // final state (chunk_state_fwd.py:448-597 computes the same per sequence)
     const Span sp = span_at(a, c);
-    float* const vdst = sp.vslot >= 0 ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
+    float* const vdst = (sp.vslot >= 0 && DBG_IN(sp.vslot, a.num_seqs, 8))
+                            ? a.varlen_states + ((int64_t)sp.vslot * a.H + h) * PT * NT : nullptr;
     TRACE(5, c, 0);
     if (more && !chunk_decay<NT, HAS_SEQ>(a, m, bi, c + 1, r, prev_end, decay, sd_next)) return;
     // With one Yi buffer MMA3(c) writes Yi after the output of c-1 has read it, so that
@@ -960,7 +985,7 @@ __device__ void state_worker(const TcArgs& a, uint8_t* sm, Misc* m, int bi, int 
           sv[i + 1] = d2.y;
         }
         ptx::tmem_st32(tl + G_::COL_ST + 64 * hh + 32 * half, sv);
-      } else if (fin) {
+      } else if (fin && DBG_IN((fbh * PT + 32 * half + 31) * NT + n, (int64_t)(a.rows / a.seg_k) * a.H * PT * NT, 9)) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) fin[(fbh * PT + 32 * half + i) * NT + n] = sv[i];
       }
@@ -1729,6 +1754,9 @@ int tc_combined_fwd(const ssd_fwd_params_t* p, unsigned* status, void* workspace
   a.dtprep = prep_out;
   a.prep_cap = (int)prep_cap(p);
   a.seg_k = k;
+  a.rows = (int)b;
+  a.num_seqs = p->num_seqs;
+  a.sched_cap = p->varlen_states ? (int)sched_cap(p) : 0;
   a.trace = trace_enabled() ? (unsigned long long*)((char*)workspace + sched_bytes(p) + prep_bytes(p) + seg_bytes(p))
                             : nullptr;
   typedef void (*KernelFn)(TcArgs);
