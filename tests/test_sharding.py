@@ -236,11 +236,15 @@ def test_sequence_parallel_algorithm_matches_oracle(world, lens):
 # ---------------------------------------------------------------------------
 # the CUDA path, two ranks on one GPU
 # ---------------------------------------------------------------------------
-def _sp_gpu_worker(rank, world, port, q, lens):
+def _sp_gpu_worker(rank, world, port, q, lens, backend="gloo"):
     import torch.distributed as dist
     from gpu_util import dev_inputs, rel_l2, to_dev
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    if backend == "nccl":   # one GPU per rank, the exchange over NCCL
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
     L, Q = 1024, 128
     cfg = S.SsdConfig("sp", 1, L, 8, 64, 2, 128, Q, "bf16", has_z=True, has_init=True, return_final=True)
     inp = S.make_ssd_inputs(cfg, 21)
@@ -267,6 +271,17 @@ def test_sequence_parallel_forward_two_ranks_one_gpu(lens):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     res = _run_ranks(_sp_gpu_worker, 2, lens)
+    for r in range(2):
+        assert res[r][0] <= 1e-2, (r, res[r])
+        assert res[r][1] <= 1e-2, (r, res[r])
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("lens", [None, [300, 212, 512]], ids=["one-seq", "new-seq-at-segment"])
+def test_sequence_parallel_forward_two_gpus_nccl(lens):
+    """The same check with one GPU per rank and the state exchange over NCCL."""
+    res = _run_ranks(_sp_gpu_worker, 2, lens, "nccl")
     for r in range(2):
         assert res[r][0] <= 1e-2, (r, res[r])
         assert res[r][1] <= 1e-2, (r, res[r])
