@@ -433,6 +433,10 @@ def run_sp(args, cfg, rank, world, device):
     seq = torch.from_numpy(seq_full[t0:t1][None].copy()).to(device)
     prev = torch.tensor([int(seq_full[t0 - 1]) if t0 > 0 else 0], dtype=torch.int32, device=device)
 
+    from mamba2_b200.kernels.ssd_combined import _fwd_params
+    pf, _keep = _fwd_params(x, dt, A, B, C, Q, D, None, dt_bias, None, seq, None, True, (0.0, math.inf), 0)
+    fwd_launches = _lib.load().ssd_combined_num_launches(pf)
+
     def step(_i):
         return SH.ssd_forward_sequence_parallel(x, dt, A, B, C, Q, D=D, dt_bias=dt_bias, seq_idx=seq,
                                                 prev_seq=prev, dt_softplus=True)
@@ -460,7 +464,8 @@ def run_sp(args, cfg, rank, world, device):
                        "ngroups": G, "dstate": N, "chunk_size": Q, "packed_sequences": cfg.varlen_seqs,
                        "parallelism": f"sequence-parallel x{world}: zero-state segment forward, recursive-"
                                       f"doubling state exchange over NCCL, tensor-core fix-up"},
-            "gpu_launches": None, "clocks": clocks}
+            # per step on a rank after the first: the forward, chunk_cumsum, the fix-up
+            "gpu_launches": (fwd_launches + 2) * args.steps, "clocks": clocks}
     print(json.dumps(line), flush=True)
 
 
