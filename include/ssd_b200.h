@@ -82,14 +82,16 @@ typedef struct ssd_fwd_params {
 } ssd_fwd_params_t;
 
 /* flags */
-#define SSD_FLAG_FORCE_SIMT   1  /* use the fp32 CUDA-core pipeline even for bf16 inputs */
+#define SSD_FLAG_FORCE_SIMT   1  /* use the staged pipeline on the CUDA cores only (exact
+                                    fp32 FFMA stages), for any input dtype */
 #define SSD_FLAG_ROUND_STATES 2  /* round passed chunk states to the input dtype before
                                     chunk_scan, as ssd_combined.py:140 does */
 #define SSD_FLAG_BF16_MMA     4  /* fp32 inputs: round x, B, C (and z) to bf16 into the
                                     workspace and run the tensor-core pipeline, as the
                                     reference's Pallas kernels do for fp32 inputs (bf16 MMA
                                     operands, fp32 accumulation); without it fp32 inputs run
-                                    exact fp32 on the CUDA cores */
+                                    the staged pipeline with split-bf16 tensor-core stages
+                                    (relative error about 1e-5) */
 #define SSD_FLAG_TEST_WAIT_TIMEOUT 8  /* test only: every CTA of the fused tensor-core kernel
                                     first runs a short bounded wait on a barrier that nothing
                                     arrives on, so the wait gives up, the status word records
@@ -114,9 +116,11 @@ int ssd_status_copy_async(const void* workspace, uint32_t* dst, ssd_stream_t str
  * description in ssd_last_error().  No reference counterpart (see above). */
 int ssd_status_decode(uint32_t word);
 
-/* 1 if ssd_combined_fwd runs the tcgen05 tensor-core pipeline for these params, else 0
- * (fp32 CUDA-core pipeline).  No reference counterpart: introspection for callers that
- * size graphs or report which path ran. */
+/* 1 if ssd_combined_fwd runs the fused tcgen05 pipeline (bf16 MMA operands) for these
+ * params, else 0: the staged five-launch pipeline, whose chunk_state, bmm_chunk and
+ * chunk_scan run on the tensor cores with split-bf16 operands for fp32 inputs of a
+ * supported shape (ssd_set_fp32_stage_path) and on the CUDA cores otherwise.  No reference
+ * counterpart: introspection for callers that size graphs or report which path ran. */
 int ssd_combined_uses_tensor_cores(const ssd_fwd_params_t* p);
 
 /* Number of kernel launches one ssd_combined_fwd call enqueues for these params.
@@ -339,6 +343,15 @@ const char* ssd_last_error(void);
 
 /* SSD_B200_ABI_VERSION of the loaded library. */
 int ssd_abi_version(void);
+
+/* Process-wide choice of the kernels behind chunk_state, bmm_chunk and chunk_scan for fp32
+ * inputs, in ssd_combined_fwd's staged pipeline and in the three stage entry points:
+ * 0 (default) = tcgen05 MMAs on split-bf16 operands (hi + lo, three products each, fp32
+ * accumulation) where the shape allows (headdim a multiple of 32 up to 256, dstate a
+ * multiple of 16, 16-byte aligned rows), 1 = fp32 FFMA on the CUDA cores.  Returns the
+ * previous choice, or -1 (and ssd_last_error says why) for any other value.  No reference counterpart (its stages are
+ * Pallas kernels with one operand precision). */
+int ssd_set_fp32_stage_path(int32_t path);
 
 #ifdef __cplusplus
 }

@@ -9,11 +9,17 @@
 #include "common.cuh"
 #include "ssd_kernels.h"
 #include "ssd_tc.h"
+#include "ssd_x3.h"
+#include <atomic>
 
 namespace {
 using ssd::bf16;
 
 thread_local char g_err[512] = "";
+
+// Stage kernels for fp32 inputs: 0 = tensor cores (split-bf16) where the shape allows,
+// 1 = CUDA cores always (ssd_set_fp32_stage_path).
+std::atomic<int> g_fp32_stage_path{0};
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -157,6 +163,15 @@ const char* ssd_last_error(void) { return g_err; }
 
 int ssd_abi_version(void) { return SSD_B200_ABI_VERSION; }
 
+int ssd_set_fp32_stage_path(int32_t path) {
+  g_err[0] = 0;
+  if (path != 0 && path != 1) {
+    fail(SSD_ERR_INVALID_ARG, "path must be 0 (tensor cores) or 1 (CUDA cores)");
+    return -1;
+  }
+  return g_fp32_stage_path.exchange(path);
+}
+
 size_t ssd_combined_workspace_bytes(const ssd_fwd_params_t* p) {
   if (!p) return 0;
   {
@@ -261,20 +276,36 @@ int ssd_combined_fwd(const ssd_fwd_params_t* p, void* workspace, size_t workspac
   if ((s = cuda_status(ssd::launch_chunk_cumsum(p->dt, p->dt_dtype, p->A, p->dt_bias, p->dt_softplus,
                                                 p->dt_min, p->dt_max, b, L, H, Q, dA, dt, st), "chunk_cumsum")))
     return s;
-  if ((s = cuda_status(ssd::launch_chunk_state(p->x, p->B, p->dtype, dt, dA, p->seq_idx, b, L, H, P, G, N, Q,
-                                               states, st), "chunk_state")))
-    return s;
+  const bool x3 = !(p->flags & SSD_FLAG_FORCE_SIMT) && g_fp32_stage_path.load() == 0;
+  if (x3 && ssd::x3_chunk_state_supported(p->x, p->B, p->dtype, P, N, Q))
+    s = cuda_status(ssd::launch_x3_chunk_state((const float*)p->x, (const float*)p->B, dt, dA, p->seq_idx, b, L, H,
+                                               P, G, N, Q, states, status, st), "x3_chunk_state");
+  else
+    s = cuda_status(ssd::launch_chunk_state(p->x, p->B, p->dtype, dt, dA, p->seq_idx, b, L, H, P, G, N, Q,
+                                            states, st), "chunk_state");
+  if (s) return s;
   if ((s = cuda_status(ssd::launch_state_passing(states, dA + (Q - 1), nc * Q, Q, p->initial_states, p->seq_idx,
                                                  b, nc, H, P * N, L, Q, passed, passed_dtype,
                                                  p->final_states, st), "state_passing")))
     return s;
-  if ((s = cuda_status(ssd::launch_bmm_chunk(p->C, p->B, p->dtype, p->seq_idx, 0, b, L, G, N, Q, cb, st),
-                       "bmm_chunk")))
-    return s;
-  if ((s = cuda_status(ssd::launch_chunk_scan(cb, p->x, p->dtype, dt, dA, p->C, passed, passed_dtype, p->D,
-                                              p->D_ndim, p->z, p->seq_idx, b, L, H, P, G, N, Q, p->out,
-                                              p->out_x, st), "chunk_scan")))
-    return s;
+  if (x3 && ssd::x3_bmm_supported(p->C, p->B, p->dtype, N, Q))
+    // causal: chunk_scan reads CB only at k <= m, so tiles above the diagonal need no MMAs
+    s = cuda_status(ssd::launch_x3_bmm((const float*)p->C, (const float*)p->B, p->seq_idx, 1, b, L, G, N, Q, cb,
+                                       status, st), "x3_bmm_chunk");
+  else
+    s = cuda_status(ssd::launch_bmm_chunk(p->C, p->B, p->dtype, p->seq_idx, 0, b, L, G, N, Q, cb, st), "bmm_chunk");
+  if (s) return s;
+  if (x3 && ssd::x3_chunk_scan_supported(p->x, p->C, p->z, cb, passed, p->dtype, passed_dtype, P, N, Q, p->out,
+                                         p->out_x))
+    s = cuda_status(ssd::launch_x3_chunk_scan(cb, (const float*)p->x, dt, dA, (const float*)p->C,
+                                              (const float*)passed, p->D, p->D_ndim, (const float*)p->z,
+                                              p->seq_idx, b, L, H, P, G, N, Q, p->out, p->out_x, status, st),
+                    "x3_chunk_scan");
+  else
+    s = cuda_status(ssd::launch_chunk_scan(cb, p->x, p->dtype, dt, dA, p->C, passed, passed_dtype, p->D, p->D_ndim,
+                                           p->z, p->seq_idx, b, L, H, P, G, N, Q, p->out, p->out_x, st),
+                    "chunk_scan");
+  if (s) return s;
   if (p->varlen_states) {
     if ((s = cuda_status(ssd::launch_chunk_state_varlen(p->B, p->x, p->dtype, dt, dA, p->cu_seqlens, p->num_seqs,
                                                         passed, passed_dtype, L, H, P, G, N, Q,
@@ -307,6 +338,10 @@ int ssd_chunk_state_fwd(const void* x, const void* B, int32_t dtype, const float
   if (s) return s;
   if (!x || !B || !dt_out || !dA_cumsum || !states) return fail(SSD_ERR_INVALID_ARG, "null pointer");
   if (!dtype_ok(dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (g_fp32_stage_path.load() == 0 && ssd::x3_chunk_state_supported(x, B, dtype, headdim, dstate, chunk_size))
+    return cuda_status(ssd::launch_x3_chunk_state((const float*)x, (const float*)B, dt_out, dA_cumsum, seq_idx, batch,
+                                                  seqlen, nheads, headdim, ngroups, dstate, chunk_size, states,
+                                                  nullptr, (cudaStream_t)stream), "x3_chunk_state");
   return cuda_status(ssd::launch_chunk_state(x, B, dtype, dt_out, dA_cumsum, seq_idx, batch, seqlen, nheads,
                                              headdim, ngroups, dstate, chunk_size, states,
                                              (cudaStream_t)stream), "chunk_state");
@@ -341,6 +376,9 @@ int ssd_bmm_chunk_fwd(const void* a, const void* b, int32_t dtype, const int32_t
   if (s) return s;
   if (!a || !b || !out) return fail(SSD_ERR_INVALID_ARG, "null pointer");
   if (!dtype_ok(dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
+  if (g_fp32_stage_path.load() == 0 && ssd::x3_bmm_supported(a, b, dtype, k, chunk_size))
+    return cuda_status(ssd::launch_x3_bmm((const float*)a, (const float*)b, seq_idx, causal, batch, seqlen, ngroups,
+                                          k, chunk_size, out, nullptr, (cudaStream_t)stream), "x3_bmm_chunk");
   return cuda_status(ssd::launch_bmm_chunk(a, b, dtype, seq_idx, causal, batch, seqlen, ngroups, k, chunk_size,
                                            out, (cudaStream_t)stream), "bmm_chunk");
 }
@@ -357,6 +395,12 @@ int ssd_chunk_scan_fwd(const float* cb, const void* x, int32_t dtype, const floa
   if (!dtype_ok(dtype) || !dtype_ok(states_dtype)) return fail(SSD_ERR_INVALID_ARG, "bad dtype enum");
   if (D_ndim < 0 || D_ndim > 2 || (D_ndim && !D)) return fail(SSD_ERR_INVALID_ARG, "bad D_ndim / D");
   if (out_x && !z) return fail(SSD_ERR_INVALID_ARG, "out_x requires z");
+  if (g_fp32_stage_path.load() == 0 &&
+      ssd::x3_chunk_scan_supported(x, C, z, cb, states, dtype, states_dtype, headdim, dstate, chunk_size, out, out_x))
+    return cuda_status(ssd::launch_x3_chunk_scan(cb, (const float*)x, dt_out, dA_cumsum, (const float*)C,
+                                                 (const float*)states, D, D_ndim, (const float*)z, seq_idx, batch,
+                                                 seqlen, nheads, headdim, ngroups, dstate, chunk_size, out, out_x,
+                                                 nullptr, (cudaStream_t)stream), "x3_chunk_scan");
   return cuda_status(ssd::launch_chunk_scan(cb, x, dtype, dt_out, dA_cumsum, C, states, states_dtype, D, D_ndim,
                                             z, seq_idx, batch, seqlen, nheads, headdim, ngroups, dstate,
                                             chunk_size, out, out_x, (cudaStream_t)stream), "chunk_scan");

@@ -14,45 +14,47 @@ constexpr int TM = 64, TN = 64, TK = 32, NT = 256, PADW = TM + 1;
 
 // ---------------------------------------------------------------------------
 // Stage 1: chunk_cumsum (chunk_cumsum_fwd.py:194-235; ssd_naive.py:66-68 order:
-// dA = dt*A, then an inclusive scan inside the chunk).
-// grid (nc, b, ceil(H/32)), 256 threads; dynamic smem Q*33 floats.
+// dA = dt*A, then an inclusive scan inside the chunk).  One warp per (batch, head, chunk):
+// lane l owns positions [l*per, (l+1)*per) (per = Q/32 <= 8), loads them all at once, scans
+// them serially and adds the warp's exclusive prefix.  grid ceil(b*H*nc / 8), 256 threads.
 // ---------------------------------------------------------------------------
 template <typename TDT>
 __global__ void __launch_bounds__(NT) chunk_cumsum_kernel(
     const TDT* __restrict__ dt, const float* __restrict__ A, const float* __restrict__ dt_bias,
-    int softplus, float lo, float hi, int L, int H, int Q, int nc,
+    int softplus, float lo, float hi, int L, int H, int Q, int nc, int64_t nwarps,
     float* __restrict__ dA_cs, float* __restrict__ dt_out) {
-  extern __shared__ float s[];
-  const int c = blockIdx.x, bi = blockIdx.y, h0 = blockIdx.z * 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int h = h0 + lane;
-  const float bias = (dt_bias && h < H) ? dt_bias[h] : 0.f;
-  for (int q = warp; q < Q; q += NT / 32) {
-    const int64_t pos = (int64_t)c * Q + q;
-    float v = 0.f;
-    if (pos < L && h < H) v = dt_process(ldg(dt + ((int64_t)bi * L + pos) * H + h), bias, softplus, lo, hi);
-    s[q * 33 + lane] = v;
-  }
-  __syncthreads();
+  const int64_t wid = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
+  if (wid >= nwarps) return;
+  const int lane = threadIdx.x & 31;
+  const int c = wid % nc;
+  const int h = (wid / nc) % H;
+  const int bi = wid / ((int64_t)nc * H);
   const int per = Q / 32;
-  for (int hh = warp; hh < 32; hh += NT / 32) {
-    const int hd = h0 + hh;
-    if (hd >= H) break;
-    const float a = A[hd];
-    float loc[8];
-    float run = 0.f;
+  const float bias = dt_bias ? dt_bias[h] : 0.f;
+  const float a = A[h];
+  float v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < per) { run += s[(lane * per + j) * 33 + hh] * a; loc[j] = run; }
-    const float excl = warp_incl_scan(run) - run;
-    const int64_t base = (((int64_t)bi * H + hd) * nc + c) * Q + lane * per;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < per) {
-        dA_cs[base + j] = loc[j] + excl;
-        dt_out[base + j] = s[(lane * per + j) * 33 + hh];
-      }
+  for (int j = 0; j < 8; ++j) {
+    const int64_t pos = (int64_t)c * Q + lane * per + j;
+    v[j] = (j < per && pos < L) ? ldg(dt + ((int64_t)bi * L + pos) * H + h) : 0.f;
   }
+  float loc[8];
+  float run = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t pos = (int64_t)c * Q + lane * per + j;
+    v[j] = (j < per && pos < L) ? dt_process(v[j], bias, softplus, lo, hi) : 0.f;
+    run += v[j] * a;
+    loc[j] = run;
+  }
+  const float excl = warp_incl_scan(run) - run;
+  const int64_t base = (((int64_t)bi * H + h) * nc + c) * Q + lane * per;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j < per) {
+      dA_cs[base + j] = loc[j] + excl;
+      dt_out[base + j] = v[j];
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -154,25 +156,40 @@ __global__ void __launch_bounds__(NT) state_passing_kernel(
     for (int j = 0; j < cnt; ++j) run[j] = init[bh * dim + d0 + j];
   int prev_seq = 0;
   const float* dAp = dA_chunk + bh * stride_bh;
-  for (int c = 0; c < nc; ++c) {
-    const int64_t off = (((int64_t)bi * nc + c) * H + h) * dim + d0;
-    float s[4];
-    if (cnt == 4 && ((off & 3) == 0)) {
-      const float4 v = *reinterpret_cast<const float4*>(states + off);
-      s[0] = v.x; s[1] = v.y; s[2] = v.z; s[3] = v.w;
-    } else {
-      for (int j = 0; j < 4; ++j) s[j] = j < cnt ? states[off + j] : 0.f;
+  // Eight chunks' states and decays are loaded before any of them is written back: out may
+  // alias states, but the write of chunk c only replaces what was read for chunk c.
+  constexpr int DEPTH = 8;
+  for (int c0 = 0; c0 < nc; c0 += DEPTH) {
+    float s[DEPTH][4], scale[DEPTH];
+#pragma unroll
+    for (int q = 0; q < DEPTH; ++q) {
+      const int c = c0 + q;
+      if (c >= nc) break;
+      const int64_t off = (((int64_t)bi * nc + c) * H + h) * dim + d0;
+      if (cnt == 4 && ((off & 3) == 0)) {
+        const float4 v = *reinterpret_cast<const float4*>(states + off);
+        s[q][0] = v.x; s[q][1] = v.y; s[q][2] = v.z; s[q][3] = v.w;
+      } else {
+        for (int j = 0; j < 4; ++j) s[q][j] = j < cnt ? states[off + j] : 0.f;
+      }
+      scale[q] = dAp[c * stride_c];
     }
-    float scale = expf(dAp[c * stride_c]);
-    if (seq_idx) {
-      const int64_t e = min((int64_t)(c + 1) * Q, L) - 1;
-      const int cur = seq_idx[(int64_t)bi * L + e];
-      if (cur != prev_seq) scale = 0.f;
-      prev_seq = cur;
-    }
-    for (int j = 0; j < cnt; ++j) {
-      st(out + off + j, run[j]);
-      run[j] = scale * run[j] + s[j];
+#pragma unroll
+    for (int q = 0; q < DEPTH; ++q) {
+      const int c = c0 + q;
+      if (c >= nc) break;
+      const int64_t off = (((int64_t)bi * nc + c) * H + h) * dim + d0;
+      float sc = expf(scale[q]);
+      if (seq_idx) {
+        const int64_t e = min((int64_t)(c + 1) * Q, L) - 1;
+        const int cur = seq_idx[(int64_t)bi * L + e];
+        if (cur != prev_seq) sc = 0.f;
+        prev_seq = cur;
+      }
+      for (int j = 0; j < cnt; ++j) {
+        st(out + off + j, run[j]);
+        run[j] = sc * run[j] + s[q][j];
+      }
     }
   }
   if (final_states)
@@ -466,14 +483,14 @@ cudaError_t launch_chunk_cumsum(const void* dt, int dt_dtype, const float* A, co
                                 int softplus, float lo, float hi, int64_t b, int64_t L, int64_t H,
                                 int64_t Q, float* dA_cs, float* dt_out, cudaStream_t st) {
   const int nc = (int)((L + Q - 1) / Q);
-  dim3 grid(nc, (unsigned)b, cdiv(H, 32));
-  const size_t smem = (size_t)Q * 33 * sizeof(float);
+  const int64_t nw = b * H * nc;
+  const unsigned grid = cdiv(nw, NT / 32);
   if (dt_dtype == SSD_DTYPE_BF16)
-    chunk_cumsum_kernel<bf16><<<grid, NT, smem, st>>>((const bf16*)dt, A, dt_bias, softplus, lo, hi,
-                                                      (int)L, (int)H, (int)Q, nc, dA_cs, dt_out);
+    chunk_cumsum_kernel<bf16><<<grid, NT, 0, st>>>((const bf16*)dt, A, dt_bias, softplus, lo, hi, (int)L, (int)H,
+                                                   (int)Q, nc, nw, dA_cs, dt_out);
   else
-    chunk_cumsum_kernel<float><<<grid, NT, smem, st>>>((const float*)dt, A, dt_bias, softplus, lo, hi,
-                                                       (int)L, (int)H, (int)Q, nc, dA_cs, dt_out);
+    chunk_cumsum_kernel<float><<<grid, NT, 0, st>>>((const float*)dt, A, dt_bias, softplus, lo, hi, (int)L, (int)H,
+                                                    (int)Q, nc, nw, dA_cs, dt_out);
   return cudaGetLastError();
 }
 

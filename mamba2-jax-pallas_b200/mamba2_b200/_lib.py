@@ -37,7 +37,7 @@ EXPORTED = ["ssd_combined_workspace_bytes", "ssd_combined_uses_tensor_cores",
             "ssd_chunk_state_fwd", "ssd_state_passing_fwd", "ssd_bmm_chunk_fwd",
             "ssd_chunk_scan_fwd", "ssd_chunk_state_varlen_fwd", "ssd_selective_state_update",
             "ssd_causal_conv1d_fwd", "ssd_causal_conv1d_update", "ssd_rms_norm_gated", "ssd_sp_state_fixup", "ssd_status_copy_async", "ssd_status_decode",
-            "ssd_last_error", "ssd_abi_version"]
+            "ssd_last_error", "ssd_abi_version", "ssd_set_fp32_stage_path"]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -148,6 +148,7 @@ def load() -> ctypes.CDLL:
     lib.ssd_selective_state_update.argtypes = [P(SsuParams), _vp]
     lib.ssd_status_copy_async.argtypes = [_vp, _vp, _vp]
     lib.ssd_status_decode.argtypes = [ctypes.c_uint32]
+    lib.ssd_set_fp32_stage_path.argtypes = [_i32]
     for name in EXPORTED:
         if name not in ("ssd_last_error", "ssd_abi_version", "ssd_combined_workspace_bytes"):
             getattr(lib, name).restype = ctypes.c_int
@@ -162,6 +163,32 @@ def check(code: int) -> None:
     if code != 0:
         msg = load().ssd_last_error().decode(errors="replace")
         raise SsdError(code, msg)
+
+
+FP32_STAGES_TENSOR_CORES = 0
+FP32_STAGES_CUDA_CORES = 1
+
+
+class fp32_stage_path:
+    """Choose the kernels behind chunk_state, bmm_chunk and chunk_scan for fp32 inputs
+    (process-wide, ssd_set_fp32_stage_path): FP32_STAGES_TENSOR_CORES (default; split-bf16
+    tcgen05 MMAs) or FP32_STAGES_CUDA_CORES (fp32 FFMA).  A context manager that puts the
+    previous choice back on exit."""
+
+    def __init__(self, path: int):
+        self.path = path
+        self.prev = None
+
+    def __enter__(self):
+        r = load().ssd_set_fp32_stage_path(self.path)
+        if r < 0:
+            raise SsdError(1, load().ssd_last_error().decode(errors="replace"))
+        self.prev = r
+        return self
+
+    def __exit__(self, *exc):
+        load().ssd_set_fp32_stage_path(self.prev)
+        return False
 
 
 def check_device_status(workspace: torch.Tensor, stream=None) -> None:

@@ -93,7 +93,8 @@ def test_combined_return_conventions():
     assert v.shape == (2, 2, 64, 64)
     o, f, v = mamba_chunk_scan_combined_fwd(*a, seq_idx=seq.int(), cu_seqlens=cu,
                                             return_final_states=True, return_varlen_states=True)
-    torch.testing.assert_close(f[0], v[1], rtol=1e-5, atol=1e-5)
+    # two different kernels reach the same state (fp32 contract: 1e-4)
+    torch.testing.assert_close(f[0], v[1], rtol=1e-4, atol=1e-4)
 
 
 # ---------------------------------------------------------------------------
@@ -122,6 +123,19 @@ def test_chunk_cumsum(dtype, L, Q):
         assert (dto.reshape(2, 40, -1)[:, :, L:] == 0).all()
 
 
+# fp32 stage kernels: "tc" = split-bf16 tcgen05 (default), "cuda" = fp32 FFMA.  bf16 inputs
+# always take the CUDA-core stages, so they run once.  Tolerance: the FFMA stages are exact
+# fp32 (1e-5); the split-bf16 products carry about 1e-5 relative error each (4e-5 here,
+# inside the fp32 contract of 1e-4).
+STAGE_PATHS = [("f32", "tc"), ("f32", "cuda"), ("bf16", "cuda")]
+STAGE_TOL = {"tc": 4e-5, "cuda": 1e-5}
+
+
+def _stage_path(path):
+    import mamba2_b200._lib as L
+    return L.fp32_stage_path(L.FP32_STAGES_TENSOR_CORES if path == "tc" else L.FP32_STAGES_CUDA_CORES)
+
+
 SEQ_CFGS = [None, [[256]], [[128, 128]], [[200, 312], [100, 412]],
             [[64, 192, 256], [128, 128, 256]], [[64, 64, 64, 64]]]
 
@@ -136,9 +150,9 @@ def _seq_idx(batch, L, lens):
     return out
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype,path", STAGE_PATHS)
 @pytest.mark.parametrize("lens", SEQ_CFGS)
-def test_chunk_state(dtype, lens):
+def test_chunk_state(dtype, path, lens):
     from mamba2_b200 import chunk_state_fwd
     batch = 1 if lens is None else len(lens)
     L = 512 if lens is None else sum(lens[0])
@@ -146,9 +160,10 @@ def test_chunk_state(dtype, lens):
     inp, dA, dto = _stage_inputs(cfg)
     seq = None if lens is None else _seq_idx(batch, L, lens)
     ref = R.chunk_state(inp["B"], inp["x"], dto, dA, seq)
-    got = chunk_state_fwd(to_dev(inp["x"], dtype), to_dev(inp["B"], dtype), to_dev(dto), to_dev(dA),
-                          seq_idx=to_dev(seq, int32=True))
-    assert rel_l2(got, ref) <= 1e-5
+    with _stage_path(path):
+        got = chunk_state_fwd(to_dev(inp["x"], dtype), to_dev(inp["B"], dtype), to_dev(dto), to_dev(dA),
+                              seq_idx=to_dev(seq, int32=True))
+    assert rel_l2(got, ref) <= STAGE_TOL[path]
     if seq is not None:
         # positions outside the chunk-end sequence contribute nothing (bit-exact mask):
         zero_chunks = ~R.mask_chunk_state(seq, 64).any(-1)
@@ -179,11 +194,11 @@ def test_state_passing(b, nc, H, dim, init, lens, out_dtype):
     assert rel_l2(f, f_ref) <= 1e-6
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype,path", STAGE_PATHS)
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("lens,L,Q", [(None, 512, 64), (None, 300, 128), ([[200, 312], [100, 412]], 512, 64),
                                       ([[256, 256], [128, 384]], 512, 128), ([[3, 61, 100, 92]], 256, 256)])
-def test_bmm_chunk(dtype, causal, lens, L, Q):
+def test_bmm_chunk(dtype, path, causal, lens, L, Q):
     from mamba2_b200 import bmm_chunk_fwd
     batch = 2 if lens is None else len(lens)
     rng = np.random.default_rng(L + Q)
@@ -191,18 +206,19 @@ def test_bmm_chunk(dtype, causal, lens, L, Q):
     bm = S.round_to(rng.standard_normal((batch, L, 2, 64)).astype(np.float32), dtype)
     seq = None if lens is None else _seq_idx(batch, L, lens)
     ref = R.bmm_chunk(a, bm, Q, seq, causal)
-    got = bmm_chunk_fwd(to_dev(a, dtype), to_dev(bm, dtype), Q, seq_idx=to_dev(seq, int32=True),
-                        causal=causal).cpu().numpy()
-    assert rel_l2(got, ref) <= 1e-5
+    with _stage_path(path):
+        got = bmm_chunk_fwd(to_dev(a, dtype), to_dev(bm, dtype), Q, seq_idx=to_dev(seq, int32=True),
+                            causal=causal).cpu().numpy()
+    assert rel_l2(got, ref) <= STAGE_TOL[path]
     # bit-exact mask decisions: zero exactly where the oracle mask is false
     np.testing.assert_array_equal(got == 0, ref == 0)
 
 
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("dtype,path", STAGE_PATHS)
 @pytest.mark.parametrize("lens,G,Q,Dn,z", [(None, 1, 64, 1, True), (None, 8, 64, 0, False),
                                           ([[200, 312], [100, 412]], 1, 64, 1, False),
                                           ([[256, 256], [128, 384]], 4, 128, 2, True)])
-def test_chunk_scan(dtype, lens, G, Q, Dn, z):
+def test_chunk_scan(dtype, path, lens, G, Q, Dn, z):
     """Configs of tests/test_chunk_scan_and_varlen.py:798-824."""
     from mamba2_b200 import chunk_scan_fwd
     L, H = 512, 8
@@ -216,12 +232,13 @@ def test_chunk_scan(dtype, lens, G, Q, Dn, z):
     D = np.linspace(0.5, 1.5, H * 64).reshape(H, 64).astype(np.float32) if Dn == 2 else (
         inp["D"] if Dn == 1 else None)
     o_ref, ox_ref = R.chunk_scan(CB, inp["x"], dto, dA, inp["C"], prev, D, inp["z"], seq)
-    o, ox = chunk_scan_fwd(to_dev(CB), to_dev(inp["x"], dtype), to_dev(dto), to_dev(dA),
-                           to_dev(inp["C"], dtype), to_dev(prev), D=to_dev(D),
-                           z=to_dev(inp["z"], dtype), seq_idx=to_dev(seq, int32=True))
-    assert rel_l2(o, o_ref) <= 1e-5
+    with _stage_path(path):
+        o, ox = chunk_scan_fwd(to_dev(CB), to_dev(inp["x"], dtype), to_dev(dto), to_dev(dA),
+                               to_dev(inp["C"], dtype), to_dev(prev), D=to_dev(D),
+                               z=to_dev(inp["z"], dtype), seq_idx=to_dev(seq, int32=True))
+    assert rel_l2(o, o_ref) <= STAGE_TOL[path]
     if z:
-        assert rel_l2(ox, ox_ref) <= 1e-5
+        assert rel_l2(ox, ox_ref) <= STAGE_TOL[path]
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
