@@ -397,8 +397,10 @@ __global__ void __launch_bounds__(NTH, PU <= 2 ? 2 : 1) x3_chunk_scan_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   __shared__ Ctl ctl;
-  __shared__ float dAk[256], dtk[256], sdec[128];
-  __shared__ int seqk[256];
+  __shared__ __align__(16) float dAk[256];
+  __shared__ __align__(16) float dtk[256];
+  __shared__ __align__(16) int seqk[256];
+  __shared__ float sdec[128];
   const int64_t bch = blockIdx.x;
   const int h = bch % H;
   const int c = (bch / H) % nc;
@@ -483,13 +485,24 @@ __global__ void __launch_bounds__(NTH, PU <= 2 ? 2 : 1) x3_chunk_scan_kernel(
             const int u = q * NTH + tid, r = u >> 3, j = u & 7, m = m0 + r, k = k0 + 8 * j;
             float v[8];
             if (m < Q && k <= m) {
+              // the unit's 8 columns' dA, dt (and seq ids) as 16-byte shared loads
               const float dm = dAk[m];
-              const int sm = seqk[m];
+              const float4 a0 = *reinterpret_cast<const float4*>(dAk + k), a1 = *reinterpret_cast<const float4*>(dAk + k + 4);
+              const float4 t0 = *reinterpret_cast<const float4*>(dtk + k), t1 = *reinterpret_cast<const float4*>(dtk + k + 4);
+              bool keep[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                v[i] = (k + i <= m && seqk[k + i] == sm)
-                           ? comp(R.a[2 * q + i / 4], i & 3) * expf(dm - dAk[k + i]) * dtk[k + i]
-                           : 0.f;
+              for (int i = 0; i < 8; ++i) keep[i] = k + i <= m;
+              if (seq_idx) {
+                const int sm = seqk[m];
+                const int4 s0 = *reinterpret_cast<const int4*>(seqk + k), s1 = *reinterpret_cast<const int4*>(seqk + k + 4);
+                keep[0] &= s0.x == sm; keep[1] &= s0.y == sm; keep[2] &= s0.z == sm; keep[3] &= s0.w == sm;
+                keep[4] &= s1.x == sm; keep[5] &= s1.y == sm; keep[6] &= s1.z == sm; keep[7] &= s1.w == sm;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float ak = comp(i < 4 ? a0 : a1, i & 3), tk = comp(i < 4 ? t0 : t1, i & 3);
+                v[i] = keep[i] ? comp(R.a[2 * q + i / 4], i & 3) * expf(dm - ak) * tk : 0.f;
+              }
             } else {
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[i] = 0.f;
