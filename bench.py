@@ -382,7 +382,8 @@ def run_ours(args, cfg, rank, world, device):
             "config": {"workload": cfg.name, "key": args.config, "batch": cfg.batch, "seqlen": cfg.seqlen,
                        "nheads": cfg.nheads, "headdim": cfg.headdim, "ngroups": cfg.ngroups,
                        "dstate": cfg.dstate, "chunk_size": cfg.chunk_size, "input_dtype": cfg.dtype,
-                       "mma_operands": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else "none (fp32 FFMA)",
+                       "mma_operands": "bf16" if (cfg.dtype == "bf16" or args.bf16_mma) else
+                       "split bf16 hi+lo, 3 products (tcgen05; CUDA-core cumsum and state passing)",
                        "parallelism": (f"replicas x{world}, no collective" if replicas else
                                        f"head-sharded x{world} on group boundaries, no collective"),
                        "heads_per_gpu": sets[0]["x"].shape[2],
