@@ -677,12 +677,73 @@ def run_norm(args, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+def run_tail(args, rank, world, device):
+    """tail: the c2 layer's SSD forward plus its gated RMSNorm (norm_before_gate=False, group =
+    d_ssm / G, modules/mamba2.py:395-406), ending in the bf16 tensor the layer's out_proj takes:
+    SSD (2 launches), then rms_norm_gated writing bf16 from its own pass (1 launch).  Also
+    timed in the same run: the same with the norm writing f32 and a separate cast to bf16.
+    4 rotated input sets."""
+    import dataclasses
+    from mamba2_b200 import mamba_chunk_scan_combined_fwd, rms_norm_gated
+    cfg = dataclasses.replace(S.CONFIGS["c2"], has_z=True, has_init=False, return_final=False)
+    sets = []
+    for i in range(4):
+        inp = S.make_ssd_inputs(cfg, 100 + i + 10 * rank)
+        sets.append({k: (None if v is None else torch.from_numpy(np.ascontiguousarray(v)).to(
+            torch.bfloat16 if k in ("x", "dt", "B", "C", "z") else torch.float32).to(device))
+            for k, v in inp.items() if k in ("x", "dt", "A", "B", "C", "D", "z", "dt_bias")})
+    b, L, H, P = sets[0]["x"].shape
+    d, gs = H * P, H // cfg.ngroups * P
+    w = (1.0 + 0.1 * torch.randn(d, generator=torch.Generator().manual_seed(5))).to(device)
+
+    def ssd(t):
+        return mamba_chunk_scan_combined_fwd(t["x"], t["dt"], t["A"], t["B"], t["C"], cfg.chunk_size, D=t["D"],
+                                             dt_bias=t["dt_bias"], dt_softplus=True).view(b, L, d)
+
+    def one_pass(i):
+        t = sets[i % 4]
+        return rms_norm_gated(ssd(t), w, z=t["z"].view(b, L, d), group_size=gs, norm_before_gate=False,
+                              out_dtype=torch.bfloat16)
+
+    def with_cast(i):
+        t = sets[i % 4]
+        o = rms_norm_gated(ssd(t), w, z=t["z"].view(b, L, d), group_size=gs, norm_before_gate=False)
+        return o.to(torch.bfloat16)
+    for i in range(max(args.warmup, 3)):
+        one_pass(i)
+        with_cast(i)
+    stream = torch.cuda.current_stream()
+    steps = args.steps
+    clk = Clocks(device.index) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_region(one_pass, steps, stream)
+    clocks = clk.stop() if clk else None
+    ms2 = time_region(with_cast, steps, stream)
+    t = torch.tensor([ms, ms2], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, ms2 = (float(v) for v in t.tolist())
+    if rank != 0:
+        return
+    line = {"metric": "SSD + gated RMSNorm tokens/s", "value": steps * b * L * world / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "nemotron-h-8b SSD layer + gated RMSNorm, bf16 result", "key": "tail",
+                       "batch": b, "seqlen": L, "nheads": H, "group_size": gs, "norm_before_gate": False,
+                       "l2": "4 rotated input sets, each step's inputs+outputs > L2"},
+            "with_cast_ms_per_step": ms2 / steps,
+            "gpu_launches": 3 * steps, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4", "conv", "norm"])
+    ap.add_argument("--config", default="c2", choices=["c0", "c1", "c2", "c3", "c4", "conv", "norm", "tail"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--bf16-mma", action="store_true",
@@ -702,7 +763,7 @@ def main():
         kv = dict(o.split("=", 1) for o in args.override)
         cfg = dataclasses.replace(cfg, **{k: type(getattr(cfg, k))(v) for k, v in kv.items()})
         S.CONFIGS[args.config] = cfg
-    if args.impl == "reference" and args.config in ("c4", "conv", "norm"):
+    if args.impl == "reference" and args.config in ("c4", "conv", "norm", "tail"):
         raise SystemExit(f"reference arm for {args.config} not implemented")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -726,6 +787,8 @@ def main():
             run_conv(args, rank, world, device)
         elif args.config == "norm":
             run_norm(args, rank, world, device)
+        elif args.config == "tail":
+            run_tail(args, rank, world, device)
         elif args.sp:
             run_sp(args, cfg, rank, world, device)
         else:

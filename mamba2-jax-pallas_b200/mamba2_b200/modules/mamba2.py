@@ -86,8 +86,9 @@ class Mamba2:
     def _tail(self, y, z, z0, x0):
         """Gated RMSNorm, MLP bypass and output projection (steps 7-9)."""
         if self.rmsnorm:
+            # bf16 straight from the norm pass (out_proj's input dtype): no separate cast
             y = rms_norm_gated(y, self.norm_weight, z=z, group_size=self.d_ssm // self.ngroups,
-                               norm_before_gate=self.norm_before_gate)
+                               norm_before_gate=self.norm_before_gate, out_dtype=torch.bfloat16)
         y = y.to(torch.bfloat16)
         if self.d_mlp > 0:
             y = torch.cat([F.silu(z0.float()).to(torch.bfloat16) * x0, y], dim=-1)

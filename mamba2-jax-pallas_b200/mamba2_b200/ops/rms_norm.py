@@ -19,13 +19,16 @@ def _rows2d(t: torch.Tensor, hidden: int):
     return t2
 
 
-def rms_norm_gated(x, weight, z=None, eps=1e-5, group_size=None, norm_before_gate=True):
+def rms_norm_gated(x, weight, z=None, eps=1e-5, group_size=None, norm_before_gate=True, *, out_dtype=None):
     """RMSNorm over groups of the last axis with optional SiLU gate; ``rms_norm.py:15-92``.
 
     x (..., hidden) float32 or bfloat16; weight (hidden,); z of x's shape or None.
     norm_before_gate=True: ``x / rms * weight * silu(z)``; False: ``rms-normalise
     x * silu(z)``, then ``* weight``.  Returns x's shape in the promotion of the dtypes of x,
     weight and z (as JAX's arithmetic would), computed in float32 and rounded once.
+    Keyword-only extension: ``out_dtype`` (float32 or bfloat16) overrides that promotion, so
+    a caller that wants bf16 (the layer's out_proj input) gets it from the same pass instead
+    of a separate cast.
     """
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("x must be a CUDA tensor (no CPU path)")
@@ -37,10 +40,13 @@ def rms_norm_gated(x, weight, z=None, eps=1e-5, group_size=None, norm_before_gat
         raise ValueError(f"weight must be ({hidden},)")
     if z is not None and tuple(z.shape) != tuple(x.shape):
         raise ValueError("z must have x's shape")
-    out_dtype = x.dtype
-    for t in (weight, z):
-        if t is not None:
-            out_dtype = torch.promote_types(out_dtype, t.dtype)
+    if out_dtype is None:
+        out_dtype = x.dtype
+        for t in (weight, z):
+            if t is not None:
+                out_dtype = torch.promote_types(out_dtype, t.dtype)
+    elif out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
     x2 = _rows2d(x, hidden)
     if z is not None and not z.is_cuda:
         raise ValueError("z must be a CUDA tensor (no CPU path)")

@@ -158,3 +158,24 @@ def test_rms_norm_layer_shape_full_size():
     y_un.copy_(y)
     alt = rms_norm_gated(y_un, w, z=z, group_size=d // G)
     torch.testing.assert_close(out, alt, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nbg", [True, False])
+def test_rms_norm_bf16_out_is_the_f32_result_rounded_once(nbg):
+    """out_dtype=bfloat16 (the layer's out_proj input) gives the float32 result rounded once,
+    from the same pass: bit-identical to casting the float32 output."""
+    from mamba2_b200 import rms_norm_gated
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    g = torch.Generator(device="cuda").manual_seed(21)
+    y = torch.randn((2, 300, 2048), generator=g, device="cuda")
+    z = torch.randn((2, 300, 2048), generator=g, device="cuda").to(torch.bfloat16)
+    w = 1.0 + 0.1 * torch.randn((2048,), generator=g, device="cuda")
+    for gs in (1024, 200):   # register-cached kernel and the general one
+        o32 = rms_norm_gated(y, w, z=z, group_size=gs, norm_before_gate=nbg)
+        o16 = rms_norm_gated(y, w, z=z, group_size=gs, norm_before_gate=nbg, out_dtype=torch.bfloat16)
+        assert o32.dtype == torch.float32 and o16.dtype == torch.bfloat16
+        assert torch.equal(o16, o32.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        rms_norm_gated(y, w, z=z, group_size=1024, out_dtype=torch.float16)
