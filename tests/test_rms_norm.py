@@ -169,13 +169,13 @@ def test_rms_norm_bf16_out_is_the_f32_result_rounded_once(nbg):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     g = torch.Generator(device="cuda").manual_seed(21)
-    y = torch.randn((2, 300, 2048), generator=g, device="cuda")
-    z = torch.randn((2, 300, 2048), generator=g, device="cuda").to(torch.bfloat16)
-    w = 1.0 + 0.1 * torch.randn((2048,), generator=g, device="cuda")
-    for gs in (1024, 200):   # register-cached kernel and the general one
+    for hidden, gs in ((2048, 1024), (1200, 400)):   # register-cached kernel and the general one
+        y = torch.randn((2, 300, hidden), generator=g, device="cuda")
+        z = torch.randn((2, 300, hidden), generator=g, device="cuda").to(torch.bfloat16)
+        w = 1.0 + 0.1 * torch.randn((hidden,), generator=g, device="cuda")
         o32 = rms_norm_gated(y, w, z=z, group_size=gs, norm_before_gate=nbg)
         o16 = rms_norm_gated(y, w, z=z, group_size=gs, norm_before_gate=nbg, out_dtype=torch.bfloat16)
         assert o32.dtype == torch.float32 and o16.dtype == torch.bfloat16
         assert torch.equal(o16, o32.to(torch.bfloat16))
     with pytest.raises(ValueError):
-        rms_norm_gated(y, w, z=z, group_size=1024, out_dtype=torch.float16)
+        rms_norm_gated(y, w, z=z, group_size=400, out_dtype=torch.float16)
