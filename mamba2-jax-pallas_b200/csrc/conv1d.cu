@@ -14,6 +14,7 @@
 // across the warp), keeps the last width-1 inputs in registers and has the run's keep mask
 // in shared memory.  Other layouts take a one-thread-per-output kernel.
 #include "common.cuh"
+#include "ptx_sm100.cuh"
 #include "ssd_kernels.h"
 
 namespace ssd {
@@ -38,6 +39,14 @@ struct ConvArgs {
 };
 
 __device__ __forceinline__ float act(float v, int silu_on) { return silu_on ? silu(v) : v; }
+
+// silu(v) = v sigmoid(v) = 0.5 v (1 + tanh(v / 2)), with one tanh.approx
+__device__ __forceinline__ float silu_tanh(float v) {
+  const float h = 0.5f * v;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
 
 // keep[t] for one batch row: seq constant on [t, min(t + width - 1, L - 1)]
 __device__ __forceinline__ float keep_at(const int32_t* seq_row, int64_t t, int64_t L, int width) {
@@ -182,17 +191,34 @@ __global__ void __launch_bounds__(CL_THREADS) conv1d_cl_kernel(const ConvArgs a)
     const float kc = keep[i + W - 1];
     float xv[V], o[V];
     unpack_vec<T, V>(raw[i + W - 1], xv);
+    // channel pairs on the packed f32x2 units (each lane of fma.rn.f32x2 rounds as fmaf
+    // does, so the sums equal the scalar form bit for bit)
 #pragma unroll
-    for (int k = 0; k < V; ++k) {
-      const float xc = xv[k] * kc;
-      float acc = bias[k];
+    for (int k = 0; k < V; k += 2) {
+      const float2 xc = ptx::mul2(make_float2(xv[k], xv[k + 1]), make_float2(kc, kc));
+      float2 acc = make_float2(bias[k], bias[k + 1]);
 #pragma unroll
-      for (int j = 0; j < W - 1; ++j) acc = fmaf(w[k][j], win[j][k], acc);
-      acc = fmaf(w[k][W - 1], xc, acc);
-      o[k] = act(acc, a.silu);
+      for (int j = 0; j < W - 1; ++j)
+        acc = ptx::fma2(make_float2(w[k][j], w[k + 1][j]), make_float2(win[j][k], win[j][k + 1]), acc);
+      acc = ptx::fma2(make_float2(w[k][W - 1], w[k + 1][W - 1]), xc, acc);
+      if constexpr (sizeof(TO) == 2) {
+        // bf16 out: SiLU by one tanh.approx (relative error about 2^-11, well inside the
+        // output's rounding); f32 out keeps the exact form
+        o[k] = a.silu ? silu_tanh(acc.x) : acc.x;
+        o[k + 1] = a.silu ? silu_tanh(acc.y) : acc.y;
+      } else {
+        o[k] = act(acc.x, a.silu);
+        o[k + 1] = act(acc.y, a.silu);
+      }
 #pragma unroll
-      for (int j = 0; j + 1 < W - 1; ++j) win[j][k] = win[j + 1][k];
-      if (W > 1) win[W > 1 ? W - 2 : 0][k] = xc;
+      for (int j = 0; j + 1 < W - 1; ++j) {
+        win[j][k] = win[j + 1][k];
+        win[j][k + 1] = win[j + 1][k + 1];
+      }
+      if (W > 1) {
+        win[W > 1 ? W - 2 : 0][k] = xc.x;
+        win[W > 1 ? W - 2 : 0][k + 1] = xc.y;
+      }
     }
     store_vec<TO, V>(op + (t0 + i) * a.ot, o);
   }
